@@ -273,13 +273,18 @@ class OracleModel:
     def generate(self, *, input_ids, prompt_codes=None, max_new_frames=384, min_new_frames=4,
                  temperature=0.9, top_k=50, top_p=0.95, temperature_q0=None, top_k_q0=None,
                  top_p_q0=None, cfg_scale=1.0, uncond_input_ids=None, seed=0, request=0,
-                 speaker=None, on_step=None):
+                 speaker=None, on_step=None, timings=None):
         """The native rollout (model.py:515-621) with the draw restated by
-        oracle/sampler.c on Philox uniforms counter=(q, frame, request)."""
+        oracle/sampler.c on Philox uniforms counter=(q, frame, request).
+        ``timings`` (a dict) receives prefill_s and decode_s when given."""
+        import time
+
         cfg = self.cfg
         Q = cfg.num_codebooks
         branches = [input_ids] + ([uncond_input_ids] if cfg_scale != 1.0 else [])
+        t0 = time.perf_counter()
         states = [self.start(ids, prompt_codes, speaker) for ids in branches]
+        t1 = time.perf_counter()
         caches = [s[0] for s in states]
         hiddens = [s[1] for s in states]
         frames = []
@@ -310,5 +315,8 @@ class OracleModel:
                 break
             frames.append(row)
             hiddens = [self.advance(c, row) for c in caches]
+        if timings is not None:
+            timings["prefill_s"] = t1 - t0
+            timings["decode_s"] = time.perf_counter() - t1
         codes = np.asarray(frames, dtype=np.int64).reshape(-1, Q)
         return codes, {"stop_reason": stop, "num_frames": codes.shape[0], "cfg_scale": cfg_scale}

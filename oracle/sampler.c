@@ -10,7 +10,8 @@
  *   557-559  structural     merged[BOS] = merged[PAD] = -inf
  *   583-584  EOS            merged[EOS] = -inf unless (q == 0 and frame >= min)
  *   694-695  greedy         temperature <= 0 -> argmax (first maximal index)
- *   696      temperature    filtered = merged / temperature   (IEEE division)
+ *   696      temperature    filtered = merged / temperature   (IEEE division,
+ *                           then + 0.0f, which folds -0 into +0)
  *   697-699  top-k          cutoff = k-th largest (duplicates counted);
  *                           entries < cutoff removed, ties at the cutoff kept
  *   700-706  top-p          sort descending, cum = cumsum(softmax(sorted)),
@@ -168,7 +169,8 @@ int orc_sample(const float *cond, const float *uncond, int V, float cfg,
         free(m);
         return best;
     }
-    for (int i = 0; i < V; ++i) m[i] = m[i] / temperature;
+    /* the trailing + 0.0f folds -0 into +0 so that ordering by value is total */
+    for (int i = 0; i < V; ++i) m[i] = m[i] / temperature + 0.0f;
 
     int topk_on = top_k > 0 && top_k < V;
     float cutoff = -INFINITY;

@@ -1,0 +1,147 @@
+// Shared device/host helpers for the sm_100a decode kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/soraku_b200.h"
+
+namespace skb {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor still runs.
+// Everything before pdl_wait() may only touch data no predecessor writes
+// (weights, L2 prefetches); pdl_wait() returns once every predecessor grid has
+// completed and flushed its memory.  Every kernel calls pdl_wait()
+// unconditionally, so completion of a kernel implies completion of all
+// earlier ones.
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------- L2 prefetch
+// Up to 4 byte ranges of weights a later kernel will read.  The CTAs of the
+// issuing kernel split the union of the ranges evenly; thread 0 of each CTA
+// issues bulk L2 prefetches for its share, which proceed in the memory
+// system while the kernels in between run.
+struct PrefetchList {
+    const char* ptr[4];
+    unsigned long long bytes[4];
+    int n;
+};
+
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_share(const PrefetchList& pf, int cta, int ncta) {
+    if (threadIdx.x != 0 || pf.n <= 0) return;
+    unsigned long long total = 0;
+    for (int i = 0; i < pf.n; ++i) total += pf.bytes[i] & ~15ull;
+    // 16-byte granules keep every prefetch aligned
+    unsigned long long g_total = total >> 4;
+    unsigned long long g0 = g_total * (unsigned long long)cta / (unsigned long long)ncta;
+    unsigned long long g1 = g_total * (unsigned long long)(cta + 1) / (unsigned long long)ncta;
+    unsigned long long lo = g0 << 4, hi = g1 << 4;
+    unsigned long long base = 0;
+    for (int i = 0; i < pf.n; ++i) {
+        const unsigned long long seg = pf.bytes[i] & ~15ull;
+        unsigned long long s0 = base, s1 = base + seg;
+        base += seg;
+        if ((reinterpret_cast<uintptr_t>(pf.ptr[i]) & 15u) != 0) continue;  // bulk prefetch needs 16-B alignment
+        unsigned long long a = lo > s0 ? lo : s0;
+        unsigned long long b = hi < s1 ? hi : s1;
+        while (a < b) {
+            unsigned long long chunk = b - a;
+            if (chunk > 65536ull) chunk = 65536ull;
+            bulk_prefetch_l2(pf.ptr[i] + (a - s0), (unsigned)chunk);
+            a += chunk;
+        }
+    }
+}
+
+// ----------------------------------------------------------- vector loads
+// Weights are read once per pass: read-only path, no L1 allocation.
+__device__ __forceinline__ float4 ldg_stream(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+// Data written by other CTAs of the same grid (or a predecessor): L2 only.
+__device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ float4 ld_cg4(const float4* p) { return __ldcg(p); }
+
+// -------------------------------------------------------- warp reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+
+template <int N>
+struct Log2 {
+    static constexpr int value = N <= 1 ? 0 : 1 + Log2<(N > 1 ? N / 2 : 1)>::value;
+};
+template <>
+struct Log2<1> {
+    static constexpr int value = 0;
+};
+
+// Butterfly reduce-scatter of N (power of two, <= 32) values per lane: on
+// return, v[0] of lane l holds the warp-wide sum of value index
+// (l >> (5 - log2 N)).  N - 1 + (5 - log2 N) shuffles instead of 5 N.
+template <int N>
+__device__ __forceinline__ float butterfly_reduce(float (&v)[N], int lane) {
+    constexpr int L = Log2<N>::value;
+#pragma unroll
+    for (int step = 0; step < L; ++step) {
+        const int half = N >> (step + 1);
+        const int off = 16 >> step;
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            float send = upper ? v[i] : v[i + half];
+            float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(FULL, send, off);
+        }
+    }
+#pragma unroll
+    for (int off = 16 >> L; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(FULL, v[0], off);
+    return v[0];
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+// --------------------------------------------------------------- launching
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, bool pdl, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+inline int status_from(cudaError_t e) { return e == cudaSuccess ? SKB_OK : SKB_ERR_CUDA; }
+
+}  // namespace skb

@@ -1,0 +1,884 @@
+// Decode engine: the GraphFrameEngine replacement (graph_frame.py:23-328).
+//
+// One frame (graph_frame.py:201-272) is 16 depth steps followed by one trunk
+// step; on the GPU it is a fixed list of kernels:
+//
+//   for q in 0..15:
+//     D_up(q)     a = rmsnorm_in(rmsnorm_final(x) + prefix); act = silu(a Wg^T) * (a Wu^T)
+//     D_down(q)   y = act Wd^T + a
+//     D_cls(q)    logits = rmsnorm_out(y) table[q]^T + bias[q]
+//     D_samp(q)   CFG + mask + temperature + top-k/top-p + Philox draw -> code;
+//                 prefix += table[q][code] * scale   (q = 15: x = frame embedding)
+//   for l in 0..L-1:
+//     QKV(l)      qkv = rmsnorm(x) [Wq;Wk;Wv]^T
+//     ATTN(l)     q/k norm, RoPE, KV append, split-K GQA attention (+ combine)
+//     O(l)        x += attn Wo^T
+//     GU(l)       act = silu(n Wg^T) * (n Wu^T),  n = rmsnorm(x)
+//     DOWN(l)     x += act Wd^T                   (l = L-1: pos += 1)
+//
+// x holds the pre-final-norm residual stream of each CFG row; the final norm
+// is folded into D_up's prologue.  Kernels are chained with programmatic
+// dependent launch, and each kernel bulk-prefetches the next kernel's weights
+// into L2 before waiting on its predecessor, so HBM keeps streaming across
+// kernel boundaries.  The list is recorded once as a CUDA graph.
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <vector>
+
+#include "ops.cuh"
+#include "sampler.cuh"
+#include "trunk_api.cuh"
+
+namespace skb {
+
+struct ReqState {
+    float cfg, temp, temp_q0, top_p, top_p_q0;
+    int top_k, top_k_q0, min_new_frames, eos_rule;
+    int frame;  // frames completed (advanced by the q = Q-1 sampler)
+    int done;   // q0 drew EOS at least once
+    int pad_;
+    unsigned long long seed;
+};
+
+struct DepthSampleArgs {
+    const float* logits;  // [R][V]
+    int rows_per_req, V, q, Q, D;
+    ReqState* st;
+    const int* host_flag;
+    const float* table;
+    float scale;
+    float* prefix;  // [n_req][D]
+    float* x;       // [R][D]
+    int64_t* cur_codes;  // [n_req][Q]
+    int64_t* hist;       // [n_req][max_frames][Q]
+    int max_frames;
+    int bos, pad, eos;
+    PrefetchList pf;
+};
+
+__global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const DepthSampleArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int codes_s[32];
+    prefetch_share(a.pf, blockIdx.x, gridDim.x);
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.x, tid = threadIdx.x;
+    ReqState* st = a.st + r;
+    const int frame = __ldcg(&st->frame);
+    const bool q0 = a.q == 0;
+    SampleJob J;
+    J.cond = a.logits + (size_t)r * a.rows_per_req * a.V;
+    J.uncond = a.rows_per_req > 1 ? J.cond + a.V : nullptr;
+    J.V = a.V;
+    J.cfg_scale = st->cfg;
+    J.temperature = q0 ? st->temp_q0 : st->temp;
+    J.top_k = q0 ? st->top_k_q0 : st->top_k;
+    J.top_p = q0 ? st->top_p_q0 : st->top_p;
+    J.mask_eos = !q0 ? 1 : (st->eos_rule == 0 ? (__ldcg(a.host_flag) != 0) : (frame < st->min_new_frames));
+    J.bos = a.bos;
+    J.pad = a.pad;
+    J.eos = a.eos;
+    J.u = philox_uniform(st->seed, (uint32_t)r, (uint32_t)frame, (uint32_t)a.q);
+    const int code = sample_one(J, smem);
+    if (tid == 0) {
+        a.cur_codes[(size_t)r * a.Q + a.q] = code;
+        if (frame < a.max_frames) a.hist[((size_t)r * a.max_frames + frame) * a.Q + a.q] = code;
+        if (q0 && code == a.eos) st->done = 1;
+    }
+    float* pr = a.prefix + (size_t)r * a.D;
+    if (a.q < a.Q - 1) {
+        const float* trow = a.table + ((size_t)a.q * a.V + code) * a.D;
+        for (int i = tid; i < a.D; i += SAMPLER_THREADS) pr[i] = __ldcg(pr + i) + trow[i] * a.scale;
+    } else {
+        if (tid < a.Q) codes_s[tid] = (tid == a.q) ? code : (int)__ldcg(a.cur_codes + (size_t)r * a.Q + tid);
+        __syncthreads();
+        for (int i = tid; i < a.D; i += SAMPLER_THREADS) {
+            float acc = 0.f;
+            for (int qq = 0; qq < a.Q; ++qq) {
+                int c = codes_s[qq];
+                if (c < 0 || c >= a.V) c = 0;
+                const float v = a.table[((size_t)qq * a.V + c) * a.D + i];
+                acc = (qq == 0) ? v : acc + v;
+            }
+            acc = acc * a.scale;
+            for (int rr = 0; rr < a.rows_per_req; ++rr) a.x[((size_t)r * a.rows_per_req + rr) * a.D + i] = acc;
+            pr[i] = 0.f;
+        }
+        if (tid == 0) st->frame = frame + 1;
+    }
+}
+
+}  // namespace skb
+
+using namespace skb;
+
+struct skb_engine {
+    skb_model_desc m;
+    std::vector<const float*> lw;  // layer pointers
+    skb_engine_opts o;
+    int device = 0, nsm = 148;
+    int R = 0, rpr = 1, nreq = 0;
+    int D = 0, H = 0, KVH = 0, hd = 0, F = 0, I = 0, Q = 0, V = 0, L = 0, n_rep = 1;
+    int max_pages = 0, page_log2 = 6, S = 1, nmax = 1;
+    long long layer_floats = 0;
+    // decode state
+    float *x = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *abuf = nullptr, *y = nullptr,
+          *hidden = nullptr, *logits = nullptr, *logits_hist = nullptr, *prefix = nullptr, *part = nullptr,
+          *rope_cos = nullptr, *rope_sin = nullptr, *kv = nullptr;
+    int *pos = nullptr, *counters = nullptr, *page_table = nullptr, *err = nullptr, *host_flag = nullptr;
+    int64_t *cur_codes = nullptr, *hist = nullptr;
+    ReqState* st = nullptr;
+    // prefill scratch
+    float *pX = nullptr, *pN = nullptr, *pQKV = nullptr, *pQ = nullptr, *pA = nullptr, *pG = nullptr,
+          *spk = nullptr, *spk_in = nullptr;
+    PrefillTok* ptok = nullptr;
+    int64_t* pframes = nullptr;
+    int* pmeta = nullptr;  // row_off | row_len | row_id | gather_src | gather_dst
+    // graph
+    cudaStream_t cap_stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int graph_active = 0, graph_fpg = 0, graph_pdl = 0;
+    int debug = 0;
+    std::vector<int> frames_host, pos_host;
+    std::vector<ReqState> st_host;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(skb_engine* e, T** p, size_t n) {
+    void* ptr = nullptr;
+    if (n == 0) n = 1;
+    if (cudaMalloc(&ptr, n * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(SKB_ERR_NOMEM, "cudaMalloc of %zu bytes failed", n * sizeof(T));
+    }
+    cudaMemset(ptr, 0, n * sizeof(T));
+    e->allocs.push_back(ptr);
+    *p = reinterpret_cast<T*>(ptr);
+    return SKB_OK;
+}
+
+KVLayout kv_layout(const skb_engine* e) {
+    KVLayout k;
+    k.pool = e->kv;
+    k.page_table = e->page_table;
+    k.max_pages = e->max_pages;
+    k.page_log2 = e->page_log2;
+    k.KVH = e->KVH;
+    k.hd = e->hd;
+    k.layer_floats = e->layer_floats;
+    return k;
+}
+
+const float* LW(const skb_engine* e, int l, int which) { return e->lw[(size_t)l * SKB_LAYER_PTRS + which]; }
+enum { W_Q = 0, W_K, W_V, W_O, W_QN, W_KN, W_G, W_U, W_D, W_LN1, W_LN2 };
+
+struct WRange {
+    const char* p;
+    unsigned long long bytes;
+};
+
+// One kernel of the frame: its launcher (given the prefetch list of the next
+// kernel's weights) and the weight ranges it reads.
+struct Node {
+    std::vector<WRange> w;
+    std::function<cudaError_t(cudaStream_t, bool, const PrefetchList&)> run;
+};
+
+std::vector<WRange> gemv_ranges(const GemvArgs& a) {
+    std::vector<WRange> r;
+    const unsigned long long rowb = (unsigned long long)a.K * 4;
+    if (a.interleave) {
+        r.push_back({(const char*)a.w0, rowb * (a.N / 2)});
+        r.push_back({(const char*)a.w1, rowb * (a.N / 2)});
+    } else {
+        const int s1 = a.seg1 < a.N ? a.seg1 : a.N;
+        const int s2 = a.seg2 < a.N ? a.seg2 : a.N;
+        r.push_back({(const char*)a.w0, rowb * s1});
+        if (s2 > s1) r.push_back({(const char*)a.w1, rowb * (s2 - s1)});
+        if (a.N > s2) r.push_back({(const char*)a.w2, rowb * (a.N - s2)});
+    }
+    return r;
+}
+
+Node gemv_node(const skb_engine* e, GemvArgs a, int M, int XM, int EM) {
+    Node n;
+    n.w = gemv_ranges(a);
+    const int units = a.N / (EM == E_SWIGLU ? 2 : 1);
+    const int grid = units < e->nsm ? units : e->nsm;
+    n.run = [a, M, XM, EM, grid](cudaStream_t s, bool pdl, const PrefetchList& pf) {
+        GemvArgs b = a;
+        b.pf = pf;
+        return gemv_launch(b, M, XM, EM, grid, s, pdl);
+    };
+    return n;
+}
+
+std::vector<Node> build_frame(skb_engine* e, int n_active) {
+    std::vector<Node> nodes;
+    const int R = n_active * e->rpr;
+    const int D = e->D;
+    for (int q = 0; q < e->Q; ++q) {
+        float* lg = e->debug ? e->logits_hist + (size_t)q * e->R * e->V : e->logits;
+        {  // D_up
+            GemvArgs a = gemv_args_plain(e->x, D, 2 * e->I, D);
+            a.w0 = e->m.depth_gate;
+            a.w1 = e->m.depth_up;
+            a.interleave = 1;
+            a.nw2 = e->m.final_norm;
+            a.neps2 = e->m.rms_eps;
+            a.x2 = e->prefix;
+            a.ldx2 = D;
+            a.x2_div = e->rpr;
+            a.nw = e->m.depth_norm_in;
+            a.neps = e->m.depth_eps;
+            a.xout = e->abuf;
+            a.hout = e->hidden;
+            a.out = e->act;
+            a.ldo = e->I;
+            nodes.push_back(gemv_node(e, a, R, X_NORM_ADD_NORM, E_SWIGLU));
+        }
+        {  // D_down
+            GemvArgs a = gemv_args_plain(e->act, e->I, D, e->I);
+            a.w0 = e->m.depth_down;
+            a.resid = e->abuf;
+            a.ldr = D;
+            a.out = e->y;
+            a.ldo = D;
+            nodes.push_back(gemv_node(e, a, R, X_PLAIN, E_RESID));
+        }
+        {  // D_cls
+            GemvArgs a = gemv_args_plain(e->y, D, e->V, D);
+            a.w0 = e->m.table + (size_t)q * e->V * D;
+            a.nw = e->m.depth_norm_out;
+            a.neps = e->m.depth_eps;
+            a.bias = e->m.depth_bias + (size_t)q * e->V;
+            a.out = lg;
+            a.ldo = e->V;
+            nodes.push_back(gemv_node(e, a, R, X_RMSNORM, E_BIAS));
+        }
+        {  // D_samp
+            DepthSampleArgs a = {};
+            a.logits = lg;
+            a.rows_per_req = e->rpr;
+            a.V = e->V;
+            a.q = q;
+            a.Q = e->Q;
+            a.D = D;
+            a.st = e->st;
+            a.host_flag = e->host_flag;
+            a.table = e->m.table;
+            a.scale = e->m.frame_scale;
+            a.prefix = e->prefix;
+            a.x = e->x;
+            a.cur_codes = e->cur_codes;
+            a.hist = e->hist;
+            a.max_frames = e->o.max_frames;
+            a.bos = e->m.bos_id;
+            a.pad = e->m.pad_id;
+            a.eos = e->m.eos_id;
+            Node n;
+            n.run = [a, n_active](cudaStream_t s, bool pdl, const PrefetchList& pf) {
+                DepthSampleArgs b = a;
+                b.pf = pf;
+                return launch(depth_sample_kernel, dim3(n_active), dim3(SAMPLER_THREADS), SAMPLER_SMEM, s, pdl, b);
+            };
+            nodes.push_back(n);
+        }
+    }
+    const int qd = e->H * e->hd, kvd = e->KVH * e->hd;
+    for (int l = 0; l < e->L; ++l) {
+        {  // QKV
+            GemvArgs a = gemv_args_plain(e->x, D, qd + 2 * kvd, D);
+            a.w0 = LW(e, l, W_Q);
+            a.w1 = LW(e, l, W_K);
+            a.w2 = LW(e, l, W_V);
+            a.seg1 = qd;
+            a.seg2 = qd + kvd;
+            a.nw = LW(e, l, W_LN1);
+            a.neps = e->m.rms_eps;
+            a.out = e->qkv;
+            a.ldo = qd + 2 * kvd;
+            nodes.push_back(gemv_node(e, a, R, X_RMSNORM, E_STORE));
+        }
+        {  // ATTN
+            DecodeAttnArgs a = {};
+            a.qkv = e->qkv;
+            a.ld_qkv = qd + 2 * kvd;
+            a.qn = LW(e, l, W_QN);
+            a.kn = LW(e, l, W_KN);
+            a.eps = e->m.rms_eps;
+            a.rope_cos = e->rope_cos;
+            a.rope_sin = e->rope_sin;
+            a.pos = e->pos;
+            a.max_len = e->o.max_len;
+            a.kv = kv_layout(e);
+            a.layer = l;
+            a.H = e->H;
+            a.n_rep = e->n_rep;
+            a.S = e->S;
+            a.nmax = e->nmax;
+            a.scale = 1.0f / sqrtf((float)e->hd);
+            a.part = e->part;
+            a.counters = e->counters;
+            a.out = e->attn;
+            a.err = e->err;
+            Node n;
+            n.run = [a, R](cudaStream_t s, bool pdl, const PrefetchList& pf) {
+                DecodeAttnArgs b = a;
+                b.pf = pf;
+                return decode_attn_launch(b, R, s, pdl);
+            };
+            nodes.push_back(n);
+        }
+        {  // O
+            GemvArgs a = gemv_args_plain(e->attn, qd, D, qd);
+            a.w0 = LW(e, l, W_O);
+            a.resid = e->x;
+            a.ldr = D;
+            a.out = e->x;
+            a.ldo = D;
+            nodes.push_back(gemv_node(e, a, R, X_PLAIN, E_RESID));
+        }
+        {  // GU
+            GemvArgs a = gemv_args_plain(e->x, D, 2 * e->F, D);
+            a.w0 = LW(e, l, W_G);
+            a.w1 = LW(e, l, W_U);
+            a.interleave = 1;
+            a.nw = LW(e, l, W_LN2);
+            a.neps = e->m.rms_eps;
+            a.out = e->act;
+            a.ldo = e->F;
+            nodes.push_back(gemv_node(e, a, R, X_RMSNORM, E_SWIGLU));
+        }
+        {  // DOWN
+            GemvArgs a = gemv_args_plain(e->act, e->F, D, e->F);
+            a.w0 = LW(e, l, W_D);
+            a.resid = e->x;
+            a.ldr = D;
+            a.out = e->x;
+            a.ldo = D;
+            if (l == e->L - 1) {
+                a.inc = e->pos;
+                a.n_inc = R;
+            }
+            nodes.push_back(gemv_node(e, a, R, X_PLAIN, E_RESID));
+        }
+    }
+    return nodes;
+}
+
+PrefetchList make_pf(const std::vector<WRange>& w, bool on) {
+    PrefetchList pf = {};
+    if (!on) return pf;
+    for (size_t i = 0; i < w.size() && i < 4; ++i) {
+        pf.ptr[pf.n] = w[i].p;
+        pf.bytes[pf.n] = w[i].bytes;
+        ++pf.n;
+    }
+    return pf;
+}
+
+int run_frames(skb_engine* e, const std::vector<Node>& nodes, int frames, cudaStream_t s, bool pdl) {
+    const size_t n = nodes.size();
+    for (int f = 0; f < frames; ++f) {
+        for (size_t i = 0; i < n; ++i) {
+            const Node& nx = nodes[(i + 1) % n];
+            const PrefetchList pf = make_pf(nx.w, e->o.l2_prefetch != 0);
+            const bool use_pdl = pdl && !(f == 0 && i == 0);
+            cudaError_t err = nodes[i].run(s, use_pdl, pf);
+            if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "frame kernel %zu: %s", i, cudaGetErrorString(err));
+        }
+    }
+    return SKB_OK;
+}
+
+void destroy_graph(skb_engine* e) {
+    if (e->exec) cudaGraphExecDestroy(e->exec);
+    e->exec = nullptr;
+    e->graph_active = 0;
+    e->graph_fpg = 0;
+}
+
+int upload_state(skb_engine* e, int req, cudaStream_t s) {
+    cudaError_t err = cudaMemcpyAsync(e->st + req, &e->st_host[req], sizeof(ReqState),
+                                      cudaMemcpyHostToDevice, s);
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "state upload: %s", cudaGetErrorString(err));
+    return SKB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb_engine** out) {
+    if (!md || !opts || !out) return fail(SKB_ERR_ARG, "engine_create: null argument");
+    *out = nullptr;
+    const skb_model_desc& m = *md;
+    if (m.head_dim != 128) return fail(SKB_ERR_ARG, "head_dim must be 128 (got %d)", m.head_dim);
+    if (m.n_heads % m.n_kv_heads != 0 || m.n_heads / m.n_kv_heads > 2)
+        return fail(SKB_ERR_ARG, "GQA group size must be 1 or 2 (heads %d / kv heads %d)", m.n_heads, m.n_kv_heads);
+    if (m.d_model % 16 || m.d_model > 4096 || m.ffn_dim % 16 || m.ffn_dim > 4096 || m.depth_inner % 16 ||
+        m.depth_inner > 4096 || m.n_heads * m.head_dim > 4096)
+        return fail(SKB_ERR_ARG, "model widths must be multiples of 16 and <= 4096");
+    if (m.audio_vocab > SAMPLER_VMAX) return fail(SKB_ERR_ARG, "audio vocab %d > %d", m.audio_vocab, SAMPLER_VMAX);
+    if (m.n_codebooks > 32 || m.n_codebooks < 1) return fail(SKB_ERR_ARG, "1..32 codebooks supported");
+    if (opts->rows_per_request != 1 && opts->rows_per_request != 2)
+        return fail(SKB_ERR_ARG, "rows_per_request must be 1 or 2");
+    if (opts->max_requests < 1 || opts->max_requests * opts->rows_per_request > 4)
+        return fail(SKB_ERR_ARG, "max_requests * rows_per_request must be 1..4 for the decode GEMV");
+    if (opts->max_len < 2 || opts->max_frames < 1 || opts->max_prefill < 1 || opts->max_prefill > opts->max_len)
+        return fail(SKB_ERR_ARG, "bad capacities (max_len %d, max_frames %d, max_prefill %d)", opts->max_len,
+                    opts->max_frames, opts->max_prefill);
+    if (!m.rope_inv_freq || !m.layers || !m.embed_tokens || !m.table || !m.depth_bias || !m.final_norm)
+        return fail(SKB_ERR_ARG, "engine_create: missing weight pointers");
+    for (int i = 0; i < m.n_layers * SKB_LAYER_PTRS; ++i)
+        if (!m.layers[i] || !aligned16(m.layers[i])) return fail(SKB_ERR_ARG, "layer weight %d null or unaligned", i);
+
+    skb_engine* e = new skb_engine();
+    e->m = m;
+    e->lw.assign(m.layers, m.layers + (size_t)m.n_layers * SKB_LAYER_PTRS);
+    e->m.layers = nullptr;
+    e->o = *opts;
+    cudaGetDevice(&e->device);
+    cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, e->device);
+    e->rpr = opts->rows_per_request;
+    e->nreq = opts->max_requests;
+    e->R = e->nreq * e->rpr;
+    e->D = m.d_model;
+    e->H = m.n_heads;
+    e->KVH = m.n_kv_heads;
+    e->hd = m.head_dim;
+    e->F = m.ffn_dim;
+    e->I = m.depth_inner;
+    e->Q = m.n_codebooks;
+    e->V = m.audio_vocab;
+    e->L = m.n_layers;
+    e->n_rep = m.n_heads / m.n_kv_heads;
+    int ps = opts->page_size > 0 ? opts->page_size : 64;
+    e->page_log2 = 0;
+    while ((1 << e->page_log2) < ps) ++e->page_log2;
+    e->o.page_size = 1 << e->page_log2;
+    e->max_pages = (opts->max_len + e->o.page_size - 1) / e->o.page_size;
+    e->S = opts->attn_splits > 0 ? opts->attn_splits : (e->nsm / (e->R * e->KVH) > 0 ? e->nsm / (e->R * e->KVH) : 1);
+    e->nmax = (opts->max_len + e->S - 1) / e->S + 1;
+    if ((size_t)e->n_rep * e->nmax * 4 > 160 * 1024) {
+        delete e;
+        return fail(SKB_ERR_ARG, "max_len %d too long for %d attention splits", opts->max_len, e->S);
+    }
+    const size_t n_pages = (size_t)e->R * e->max_pages;
+    e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;
+    const int qkvd = (e->H + 2 * e->KVH) * e->hd;
+    const int actd = e->F > e->I ? e->F : e->I;
+    const int T = e->rpr * opts->max_prefill;
+    int st = SKB_OK;
+#define A(ptr, n)                          \
+    if (st == SKB_OK) st = dalloc(e, &ptr, (size_t)(n));
+    A(e->x, (size_t)e->R * e->D)
+    A(e->qkv, (size_t)e->R * qkvd)
+    A(e->attn, (size_t)e->R * e->H * e->hd)
+    A(e->act, (size_t)e->R * actd)
+    A(e->abuf, (size_t)e->R * e->D)
+    A(e->y, (size_t)e->R * e->D)
+    A(e->hidden, (size_t)e->R * e->D)
+    A(e->logits, (size_t)e->R * e->V)
+    A(e->logits_hist, (size_t)e->Q * e->R * e->V)
+    A(e->prefix, (size_t)e->nreq * e->D)
+    A(e->part, (size_t)e->R * e->KVH * e->S * e->n_rep * (e->hd + 2))
+    A(e->rope_cos, (size_t)opts->max_len * (e->hd / 2))
+    A(e->rope_sin, (size_t)opts->max_len * (e->hd / 2))
+    A(e->kv, (size_t)e->L * e->layer_floats)
+    A(e->pos, e->R)
+    A(e->counters, (size_t)e->R * e->KVH)
+    A(e->page_table, (size_t)e->R * e->max_pages)
+    A(e->err, 4)
+    A(e->host_flag, 1)
+    A(e->cur_codes, (size_t)e->nreq * e->Q)
+    A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
+    A(e->st, e->nreq)
+    A(e->pX, (size_t)T * e->D)
+    A(e->pN, (size_t)T * e->D)
+    A(e->pQKV, (size_t)T * qkvd)
+    A(e->pQ, (size_t)T * e->H * e->hd)
+    A(e->pA, (size_t)T * e->H * e->hd)
+    A(e->pG, (size_t)T * e->F)
+    A(e->spk, e->D)
+    A(e->spk_in, m.speaker_dim > 0 ? m.speaker_dim : 1)
+    A(e->ptok, T)
+    A(e->pframes, (size_t)(opts->max_prefill + 1) * e->Q)
+    A(e->pmeta, 5 * 8)
+#undef A
+    if (st != SKB_OK) {
+        skb_engine_destroy(e);
+        return st;
+    }
+    // RoPE tables: cos/sin of the fp32 angle inv_freq[i] * p (modeling_qwen3.py:130-146)
+    {
+        const int half = e->hd / 2;
+        std::vector<float> c((size_t)opts->max_len * half), s((size_t)opts->max_len * half);
+        for (int p = 0; p < opts->max_len; ++p)
+            for (int i = 0; i < half; ++i) {
+                const float ang = (float)p * m.rope_inv_freq[i];
+                c[(size_t)p * half + i] = (float)std::cos((double)ang);
+                s[(size_t)p * half + i] = (float)std::sin((double)ang);
+            }
+        cudaMemcpy(e->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(e->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+    }
+    {  // identity page table: row r owns pages [r*max_pages, (r+1)*max_pages)
+        std::vector<int> pt((size_t)e->R * e->max_pages);
+        for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
+        cudaMemcpy(e->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice);
+    }
+    e->frames_host.assign(e->nreq, 0);
+    e->pos_host.assign(e->R, 0);
+    e->st_host.assign(e->nreq, ReqState{});
+    for (auto& s : e->st_host) {
+        s.cfg = 1.5f;
+        s.temp = s.temp_q0 = 0.9f;
+        s.top_k = s.top_k_q0 = 50;
+        s.top_p = s.top_p_q0 = 0.95f;
+        s.min_new_frames = 0;
+        s.eos_rule = 0;
+    }
+    cudaMemcpy(e->st, e->st_host.data(), sizeof(ReqState) * e->nreq, cudaMemcpyHostToDevice);
+    if (cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        skb_engine_destroy(e);
+        return fail(SKB_ERR_CUDA, "stream creation failed");
+    }
+    cudaFuncSetAttribute(depth_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SAMPLER_SMEM);
+    trunk_init_attrs();
+    const cudaError_t ce = cudaDeviceSynchronize();
+    if (ce != cudaSuccess) {
+        skb_engine_destroy(e);
+        return fail(SKB_ERR_CUDA, "engine init: %s", cudaGetErrorString(ce));
+    }
+    *out = e;
+    return SKB_OK;
+}
+
+int skb_engine_destroy(skb_engine* e) {
+    if (!e) return SKB_OK;
+    destroy_graph(e);
+    if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
+    for (void* p : e->allocs) cudaFree(p);
+    delete e;
+    return SKB_OK;
+}
+
+int skb_engine_set_sampling(skb_engine* e, int req, float cfg, float temp, float temp_q0, int top_k,
+                            float top_p, int top_k_q0, float top_p_q0, uint64_t seed, int min_new_frames,
+                            int eos_rule) {
+    if (!e || req < 0 || req >= e->nreq) return fail(SKB_ERR_ARG, "set_sampling: bad request %d", req);
+    ReqState& s = e->st_host[req];
+    s.cfg = cfg;
+    s.temp = temp;
+    s.temp_q0 = temp_q0;
+    s.top_k = (top_k > 0 && top_k < e->V) ? top_k : 0;
+    s.top_k_q0 = (top_k_q0 > 0 && top_k_q0 < e->V) ? top_k_q0 : 0;
+    s.top_p = (top_p > 0.f && top_p < 1.f) ? top_p : -1.f;
+    s.top_p_q0 = (top_p_q0 > 0.f && top_p_q0 < 1.f) ? top_p_q0 : -1.f;
+    s.seed = seed;
+    s.min_new_frames = min_new_frames;
+    s.eos_rule = eos_rule;
+    // frame / done counters live on the device; upload only the parameters
+    const size_t n = offsetof(ReqState, frame);
+    cudaError_t err1 = cudaMemcpy(e->st + req, &s, n, cudaMemcpyHostToDevice);
+    cudaError_t err2 = cudaMemcpy(reinterpret_cast<char*>(e->st + req) + offsetof(ReqState, seed), &s.seed,
+                                  sizeof(s.seed), cudaMemcpyHostToDevice);
+    if (err1 != cudaSuccess || err2 != cudaSuccess) return fail(SKB_ERR_CUDA, "set_sampling upload failed");
+    return SKB_OK;
+}
+
+int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, const int64_t* uncond,
+                       int n_uncond, const int64_t* prompt, int n_prompt, const float* speaker,
+                       cudaStream_t s) {
+    if (!e || req < 0 || req >= e->nreq) return fail(SKB_ERR_ARG, "prefill: bad request");
+    if (!cond || n_cond < 1) return fail(SKB_ERR_ARG, "prefill: empty cond ids");
+    if (e->rpr == 2 && (!uncond || n_uncond < 1)) return fail(SKB_ERR_ARG, "prefill: CFG needs uncond ids");
+    if (n_prompt < 0 || (n_prompt > 0 && !prompt)) return fail(SKB_ERR_ARG, "prefill: bad prompt codes");
+    const skb_model_desc& m = e->m;
+    const bool use_spk = speaker != nullptr;
+    if (use_spk && !m.speaker_proj) return fail(SKB_ERR_ARG, "speaker embedding supplied to an unconditioned model");
+    if (!use_spk && m.speaker_proj) return fail(SKB_ERR_ARG, "this model requires a speaker embedding");
+    const bool slot = use_spk && m.speaker_slot_mode;
+    if (slot && !m.speaker_slot) return fail(SKB_ERR_ARG, "slot mode without speaker_slot_embedding");
+    // ids / codes validation
+    auto is_lang = [&](int64_t id) {
+        for (int j = 0; j < m.n_lang; ++j)
+            if (m.lang_ids[j] == id) return true;
+        return false;
+    };
+    for (int b = 0; b < e->rpr; ++b) {
+        const int64_t* ids = b == 0 ? cond : uncond;
+        const int n = b == 0 ? n_cond : n_uncond;
+        for (int i = 0; i < n; ++i)
+            if ((ids[i] < 0 || ids[i] >= m.text_vocab) && !is_lang(ids[i]))
+                return fail(SKB_ERR_ARG, "prefill: text id %lld out of range", (long long)ids[i]);
+    }
+    for (int i = 0; i < n_prompt * e->Q; ++i)
+        if (prompt[i] < 0 || prompt[i] >= e->V) return fail(SKB_ERR_ARG, "prefill: prompt code out of range");
+    std::vector<PrefillTok> toks;
+    int row_off[2] = {0, 0}, row_len[2] = {0, 0}, row_id[2] = {0, 0};
+    for (int b = 0; b < e->rpr; ++b) {
+        const int row = req * e->rpr + b;
+        const int64_t* ids = b == 0 ? cond : uncond;
+        const int n = b == 0 ? n_cond : n_uncond;
+        row_off[b] = (int)toks.size();
+        int p = 0;
+        for (int i = 0; i < n; ++i) toks.push_back({row, p++, 0, (int)ids[i]});
+        if (slot) toks.push_back({row, p++, 2, 0});
+        for (int f = 0; f <= n_prompt; ++f) toks.push_back({row, p++, 1, f});
+        row_len[b] = p;
+        row_id[b] = row;
+        if (p > e->o.max_prefill || p >= e->o.max_len)
+            return fail(SKB_ERR_CAPACITY, "prefill %d exceeds max_prefill=%d / max_len=%d", p, e->o.max_prefill,
+                        e->o.max_len);
+    }
+    const int T = (int)toks.size();
+    std::vector<int64_t> frames((size_t)(n_prompt + 1) * e->Q);
+    for (int q = 0; q < e->Q; ++q) frames[q] = m.bos_id;
+    for (int i = 0; i < n_prompt * e->Q; ++i) frames[e->Q + i] = prompt[i];
+    int meta[5 * 8] = {0};
+    for (int b = 0; b < e->rpr; ++b) {
+        meta[0 + b] = row_off[b];
+        meta[8 + b] = row_len[b];
+        meta[16 + b] = row_id[b];
+        meta[24 + b] = row_off[b] + row_len[b] - 1;
+        meta[32 + b] = row_id[b];
+    }
+    cudaError_t err = cudaSuccess;
+#define CK(x)                                                                        \
+    do {                                                                             \
+        err = (x);                                                                   \
+        if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "prefill %s: %s", #x, cudaGetErrorString(err)); \
+    } while (0)
+    CK(cudaMemcpyAsync(e->ptok, toks.data(), sizeof(PrefillTok) * T, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(e->pframes, frames.data(), frames.size() * 8, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(e->pmeta, meta, sizeof meta, cudaMemcpyHostToDevice, s));
+    const float* bos_add = nullptr;
+    if (use_spk) {
+        CK(cudaMemcpyAsync(e->spk_in, speaker, sizeof(float) * m.speaker_dim, cudaMemcpyHostToDevice, s));
+        CK(speaker_launch(e->spk_in, m.speaker_dim, m.speaker_proj, e->D, slot ? m.speaker_slot : nullptr, e->spk, s));
+        if (!slot) bos_add = e->spk;
+    }
+    CK(prefill_embed_launch(e->ptok, T, m.embed_tokens, m.text_vocab, m.lang_embed, m.n_lang, m.lang_ids,
+                            e->pframes, e->Q, m.table, e->V, m.frame_scale, e->spk, bos_add, e->pX, e->D,
+                            e->err + 1, s));
+    const KVLayout kv = kv_layout(e);
+    const int qd = e->H * e->hd, kvd = e->KVH * e->hd;
+    const int maxL = row_len[0] > row_len[1] ? row_len[0] : row_len[1];
+    for (int l = 0; l < e->L; ++l) {
+        int stt = rmsnorm_rows(e->pX, nullptr, LW(e, l, W_LN1), e->pN, T, e->D, m.rms_eps, s, false);
+        if (stt) return stt;
+        GemmArgs g = {};
+        g.A = e->pN;
+        g.lda = e->D;
+        g.w0 = LW(e, l, W_Q);
+        g.w1 = LW(e, l, W_K);
+        g.w2 = LW(e, l, W_V);
+        g.seg1 = qd;
+        g.seg2 = qd + kvd;
+        g.N = qd + 2 * kvd;
+        g.K = e->D;
+        g.T = T;
+        g.out = e->pQKV;
+        g.ldo = qd + 2 * kvd;
+        g.mode = 0;
+        CK(sgemm_launch(g, s));
+        CK(prefill_qk_launch(e->pQKV, qd + 2 * kvd, e->ptok, T, LW(e, l, W_QN), LW(e, l, W_KN), m.rms_eps,
+                             e->rope_cos, e->rope_sin, e->H, kv, l, e->pQ, s));
+        CK(prefill_attn_launch(e->pQ, e->pmeta, e->pmeta + 8, e->pmeta + 16, e->rpr, maxL, e->H, e->n_rep, kv, l,
+                               1.0f / sqrtf((float)e->hd), e->pA, s));
+        GemmArgs o = {};
+        o.A = e->pA;
+        o.lda = qd;
+        o.w0 = LW(e, l, W_O);
+        o.seg1 = o.seg2 = 1 << 30;
+        o.N = e->D;
+        o.K = qd;
+        o.T = T;
+        o.out = e->pX;
+        o.ldo = e->D;
+        o.resid = e->pX;
+        o.ldr = e->D;
+        o.mode = 1;
+        CK(sgemm_launch(o, s));
+        stt = rmsnorm_rows(e->pX, nullptr, LW(e, l, W_LN2), e->pN, T, e->D, m.rms_eps, s, false);
+        if (stt) return stt;
+        GemmArgs gu = {};
+        gu.A = e->pN;
+        gu.lda = e->D;
+        gu.w0 = LW(e, l, W_G);
+        gu.w1 = LW(e, l, W_U);
+        gu.interleave = 1;
+        gu.N = 2 * e->F;
+        gu.K = e->D;
+        gu.T = T;
+        gu.out = e->pG;
+        gu.ldo = e->F;
+        gu.mode = 3;
+        CK(sgemm_launch(gu, s));
+        GemmArgs dn = {};
+        dn.A = e->pG;
+        dn.lda = e->F;
+        dn.w0 = LW(e, l, W_D);
+        dn.seg1 = dn.seg2 = 1 << 30;
+        dn.N = e->D;
+        dn.K = e->F;
+        dn.T = T;
+        dn.out = e->pX;
+        dn.ldo = e->D;
+        dn.resid = e->pX;
+        dn.ldr = e->D;
+        dn.mode = 1;
+        CK(sgemm_launch(dn, s));
+    }
+    CK(gather_rows_launch(e->pX, e->pmeta + 24, e->pmeta + 32, e->rpr, e->x, e->D, s));
+    // positions, prefix, counters
+    int posv[2] = {row_len[0], row_len[1]};
+    CK(cudaMemcpyAsync(e->pos + req * e->rpr, posv, sizeof(int) * e->rpr, cudaMemcpyHostToDevice, s));
+    CK(cudaMemsetAsync(e->prefix + (size_t)req * e->D, 0, sizeof(float) * e->D, s));
+    int zero2[2] = {0, 0};
+    CK(cudaMemcpyAsync(reinterpret_cast<char*>(e->st + req) + offsetof(ReqState, frame), zero2, sizeof zero2,
+                       cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+#undef CK
+    for (int b = 0; b < e->rpr; ++b) e->pos_host[req * e->rpr + b] = row_len[b];
+    e->frames_host[req] = 0;
+    return SKB_OK;
+}
+
+int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream) {
+    if (!e) return fail(SKB_ERR_ARG, "capture: null engine");
+    if (n_active < 1 || n_active > e->nreq || fpg < 1 || fpg > 64)
+        return fail(SKB_ERR_ARG, "capture: n_active %d (1..%d), frames_per_graph %d (1..64)", n_active, e->nreq, fpg);
+    destroy_graph(e);
+    const std::vector<Node> nodes = build_frame(e, n_active);
+    cudaStream_t cs = e->cap_stream;
+    cudaError_t err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "capture sync: %s", cudaGetErrorString(err));
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        const bool pdl = e->o.use_pdl && attempt == 0;
+        cudaGraph_t graph = nullptr;
+        err = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+        if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "begin capture: %s", cudaGetErrorString(err));
+        int st = run_frames(e, nodes, fpg, cs, pdl);
+        err = cudaStreamEndCapture(cs, &graph);
+        if (st != SKB_OK || err != cudaSuccess) {
+            cudaGetLastError();
+            if (graph) cudaGraphDestroy(graph);
+            if (pdl) continue;
+            return st != SKB_OK ? st : fail(SKB_ERR_CUDA, "end capture: %s", cudaGetErrorString(err));
+        }
+        err = cudaGraphInstantiate(&e->exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (err != cudaSuccess) {
+            cudaGetLastError();
+            e->exec = nullptr;
+            if (pdl) continue;
+            return fail(SKB_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(err));
+        }
+        e->graph_active = n_active;
+        e->graph_fpg = fpg;
+        e->graph_pdl = pdl ? 1 : 0;
+        return SKB_OK;
+    }
+    return fail(SKB_ERR_CUDA, "capture failed");
+}
+
+static int check_capacity(skb_engine* e, int n_active, int frames) {
+    for (int r = 0; r < n_active; ++r) {
+        if (e->frames_host[r] + frames > e->o.max_frames)
+            return fail(SKB_ERR_CAPACITY, "frame buffer full (%d + %d > max_frames %d)", e->frames_host[r], frames,
+                        e->o.max_frames);
+        for (int b = 0; b < e->rpr; ++b)
+            if (e->pos_host[r * e->rpr + b] + frames > e->o.max_len)
+                return fail(SKB_ERR_CAPACITY, "KV cache full (position %d + %d > max_len %d)",
+                            e->pos_host[r * e->rpr + b], frames, e->o.max_len);
+    }
+    return SKB_OK;
+}
+
+static void advance_host(skb_engine* e, int n_active, int frames) {
+    for (int r = 0; r < n_active; ++r) {
+        e->frames_host[r] += frames;
+        for (int b = 0; b < e->rpr; ++b) e->pos_host[r * e->rpr + b] += frames;
+    }
+}
+
+int skb_engine_step(skb_engine* e, int mask_eos_q0, cudaStream_t stream) {
+    if (!e) return fail(SKB_ERR_ARG, "step: null engine");
+    if (!e->exec) return fail(SKB_ERR_STATE, "call capture() first");
+    int st = check_capacity(e, e->graph_active, e->graph_fpg);
+    if (st) return st;
+    static thread_local int flag_val;
+    flag_val = mask_eos_q0 ? 1 : 0;
+    cudaError_t err = cudaMemcpyAsync(e->host_flag, &flag_val, sizeof(int), cudaMemcpyHostToDevice, stream);
+    if (err == cudaSuccess) err = cudaGraphLaunch(e->exec, stream);
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "step: %s", cudaGetErrorString(err));
+    advance_host(e, e->graph_active, e->graph_fpg);
+    return SKB_OK;
+}
+
+int skb_engine_step_eager(skb_engine* e, int n_active, int mask_eos_q0, cudaStream_t stream) {
+    if (!e || n_active < 1 || n_active > e->nreq) return fail(SKB_ERR_ARG, "step_eager: bad arguments");
+    int st = check_capacity(e, n_active, 1);
+    if (st) return st;
+    static thread_local int flag_val;
+    flag_val = mask_eos_q0 ? 1 : 0;
+    cudaError_t err = cudaMemcpyAsync(e->host_flag, &flag_val, sizeof(int), cudaMemcpyHostToDevice, stream);
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "step_eager: %s", cudaGetErrorString(err));
+    const std::vector<Node> nodes = build_frame(e, n_active);
+    st = run_frames(e, nodes, 1, stream, false);
+    if (st) return st;
+    advance_host(e, n_active, 1);
+    return SKB_OK;
+}
+
+int skb_engine_read_codes(skb_engine* e, int req, int first, int n, int64_t* dst, cudaStream_t stream) {
+    if (!e || req < 0 || req >= e->nreq || first < 0 || n < 0 || first + n > e->o.max_frames || (n > 0 && !dst))
+        return fail(SKB_ERR_ARG, "read_codes: bad arguments");
+    if (n == 0) return SKB_OK;
+    cudaError_t err = cudaMemcpyAsync(dst, e->hist + ((size_t)req * e->o.max_frames + first) * e->Q,
+                                      sizeof(int64_t) * n * e->Q, cudaMemcpyDefault, stream);
+    return err == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "read_codes: %s", cudaGetErrorString(err));
+}
+
+int skb_engine_frames(skb_engine* e, int req) {
+    if (!e || req < 0 || req >= e->nreq) return -1;
+    return e->frames_host[req];
+}
+
+int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
+    if (!e || !ptr || !numel) return fail(SKB_ERR_ARG, "view: null argument");
+    switch (which) {
+        case 0: *ptr = e->x; *numel = (int64_t)e->R * e->D; break;
+        case 1: *ptr = e->hidden; *numel = (int64_t)e->R * e->D; break;
+        case 2: *ptr = e->logits; *numel = (int64_t)e->R * e->V; break;
+        case 3: *ptr = e->pos; *numel = e->R; break;
+        case 4: *ptr = e->logits_hist; *numel = (int64_t)e->Q * e->R * e->V; break;
+        case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
+        case 6: *ptr = e->err; *numel = 4; break;
+        case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
+        default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
+    }
+    return SKB_OK;
+}
+
+int skb_engine_set_debug(skb_engine* e, int on) {
+    if (!e) return fail(SKB_ERR_ARG, "set_debug: null engine");
+    if ((on != 0) != (e->debug != 0)) destroy_graph(e);
+    e->debug = on != 0;
+    return SKB_OK;
+}
+
+int skb_engine_kernels_per_frame(skb_engine* e) {
+    if (!e) return -1;
+    return e->Q * 4 + e->L * 5;
+}
+
+}  // extern "C"

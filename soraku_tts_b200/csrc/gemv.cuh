@@ -1,0 +1,318 @@
+// FP32 GEMV for decode: out[m, n] = epilogue(sum_k x[m, k] * W[n, k]), M <= 4
+// activation rows, W row-major [N, K] (nn.Linear layout).
+//
+// Layout on the GPU.  CTA c owns the contiguous output rows
+// [c*N/G, (c+1)*N/G) (G = grid), so its weight slice is one contiguous range
+// per weight segment and the CTAs' shares differ by at most one row.  Thread
+// t owns the K-slice of float4 columns {t, t+256, ...}: it keeps x[m, slice]
+// in registers for the whole kernel and streams W[n, slice] with 128-bit
+// loads, so each 256-thread pass reads one 4 KB weight row fully coalesced.
+// Rows are processed in chunks of RC; the RC*M partial dot products of a
+// chunk are reduced across the warp by a butterfly reduce-scatter and across
+// the 8 warps through shared memory.
+//
+// Memory-bound: 4 bytes of weight per 2*M flops; no tensor cores (FP32
+// parity with the reference's native path is required).
+#pragma once
+
+#include "common.cuh"
+
+namespace skb {
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+
+enum XMode : int {
+    X_PLAIN = 0,          // x
+    X_RMSNORM = 1,        // rmsnorm(x, nw, neps)
+    X_ADD_RMSNORM = 2,    // rmsnorm(x + x2, nw, neps)
+    X_NORM_ADD_NORM = 3,  // rmsnorm(rmsnorm(x, nw2, neps2) + x2, nw, neps)
+};
+enum EMode : int {
+    E_STORE = 0,   // out = acc
+    E_RESID = 1,   // out = acc + resid   (in place allowed: out == resid)
+    E_BIAS = 2,    // out = acc + bias[n]
+    E_SWIGLU = 3,  // logical rows interleave (gate_i, up_i): out[m, i] = silu(g) * u
+};
+
+struct GemvArgs {
+    // weights: logical rows [0, N).  interleave: row 2i -> w0 row i, 2i+1 -> w1 row i.
+    // otherwise rows [0, seg1) from w0, [seg1, seg2) from w1, [seg2, N) from w2.
+    const float* w0;
+    const float* w1;
+    const float* w2;
+    int seg1, seg2;
+    int interleave;
+    int N, K;
+    // activations [M, K] with row strides
+    const float* x;
+    int ldx;
+    const float* x2;   // addend for X_ADD_RMSNORM / X_NORM_ADD_NORM
+    int ldx2;
+    int x2_div;        // x2 row = m / x2_div (prefix shared by the rows of a request)
+    const float* nw;   // norm weight [K]
+    float neps;
+    const float* nw2;  // inner norm weight [K] (X_NORM_ADD_NORM)
+    float neps2;
+    float* xout;       // optional: CTA 0 stores the normed x [M, K] (ld = K)
+    float* hout;       // optional: CTA 0 stores the inner-normed x (X_NORM_ADD_NORM)
+    // epilogue
+    float* out;
+    int ldo;
+    const float* resid;
+    int ldr;
+    const float* bias;
+    int* inc;   // optional: CTA 0 adds 1 to inc[0 .. n_inc) after the wait (position counters)
+    int n_inc;
+    PrefetchList pf;
+};
+
+__device__ __forceinline__ const float* gemv_row(const GemvArgs& a, int r) {
+    if (a.interleave) return ((r & 1) ? a.w1 : a.w0) + (size_t)(r >> 1) * a.K;
+    if (r < a.seg1) return a.w0 + (size_t)r * a.K;
+    if (r < a.seg2) return a.w1 + (size_t)(r - a.seg1) * a.K;
+    return a.w2 + (size_t)(r - a.seg2) * a.K;
+}
+
+template <int M, int KV4>
+struct GemvShape {
+    static constexpr int RC0 = (KV4 == 1 ? 8 : (KV4 == 2 ? 4 : 2));
+    static constexpr int RC = (RC0 * M > 32) ? (32 / M) : RC0;  // rows per chunk
+    static constexpr int NV_RAW = RC * M;
+    static constexpr int NV = NV_RAW <= 2 ? 2 : (NV_RAW <= 4 ? 4 : (NV_RAW <= 8 ? 8 : (NV_RAW <= 16 ? 16 : 32)));
+};
+
+// Block-wide sum of M values (one per row); every thread gets the results.
+template <int M>
+__device__ __forceinline__ void block_sum_rows(float (&v)[M], float* red /* [GEMV_WARPS * M] */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int m = 0; m < M; ++m) v[m] = warp_sum(v[m]);
+    __syncthreads();
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) red[warp * M + m] = v[m];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < GEMV_WARPS; ++w) s += red[w * M + m];
+        v[m] = s;
+    }
+}
+
+// Loads this thread's K-slice of the M activation rows, applying the norm
+// prologue.  Columns beyond K read as zero.
+template <int M, int KV4, int XM>
+__device__ __forceinline__ void gemv_load_x(const GemvArgs& a, float4 (&xv)[M][KV4], float* red) {
+    const int tid = threadIdx.x;
+    const int K4 = a.K >> 2;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+#pragma unroll
+        for (int j = 0; j < KV4; ++j) {
+            const int k4 = tid + j * GEMV_THREADS;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k4 < K4) v = ld_cg4(reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx) + k4);
+            xv[m][j] = v;
+        }
+    }
+    if (XM == X_PLAIN) return;
+    if (XM == X_NORM_ADD_NORM) {
+        // inner norm: h = rmsnorm(x, nw2, neps2)
+        float ss[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < KV4; ++j)
+                s += xv[m][j].x * xv[m][j].x + xv[m][j].y * xv[m][j].y + xv[m][j].z * xv[m][j].z +
+                     xv[m][j].w * xv[m][j].w;
+            ss[m] = s;
+        }
+        block_sum_rows<M>(ss, red);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float inv = rsqrtf(ss[m] / (float)a.K + a.neps2);
+#pragma unroll
+            for (int j = 0; j < KV4; ++j) {
+                const int k4 = tid + j * GEMV_THREADS;
+                if (k4 < K4) {
+                    const float4 w = __ldg(reinterpret_cast<const float4*>(a.nw2) + k4);
+                    float4 v = xv[m][j];
+                    v.x = w.x * (v.x * inv);
+                    v.y = w.y * (v.y * inv);
+                    v.z = w.z * (v.z * inv);
+                    v.w = w.w * (v.w * inv);
+                    xv[m][j] = v;
+                    if (a.hout != nullptr && blockIdx.x == 0)
+                        reinterpret_cast<float4*>(a.hout + (size_t)m * a.K)[k4] = v;
+                }
+            }
+        }
+    }
+    if (XM == X_ADD_RMSNORM || XM == X_NORM_ADD_NORM) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float* x2 = a.x2 + (size_t)(m / a.x2_div) * a.ldx2;
+#pragma unroll
+            for (int j = 0; j < KV4; ++j) {
+                const int k4 = tid + j * GEMV_THREADS;
+                if (k4 < K4) {
+                    const float4 p = ld_cg4(reinterpret_cast<const float4*>(x2) + k4);
+                    xv[m][j].x += p.x;
+                    xv[m][j].y += p.y;
+                    xv[m][j].z += p.z;
+                    xv[m][j].w += p.w;
+                }
+            }
+        }
+    }
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < KV4; ++j)
+            s += xv[m][j].x * xv[m][j].x + xv[m][j].y * xv[m][j].y + xv[m][j].z * xv[m][j].z +
+                 xv[m][j].w * xv[m][j].w;
+        ss[m] = s;
+    }
+    block_sum_rows<M>(ss, red);
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const float inv = rsqrtf(ss[m] / (float)a.K + a.neps);
+#pragma unroll
+        for (int j = 0; j < KV4; ++j) {
+            const int k4 = tid + j * GEMV_THREADS;
+            if (k4 < K4) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(a.nw) + k4);
+                float4 v = xv[m][j];
+                v.x = w.x * (v.x * inv);
+                v.y = w.y * (v.y * inv);
+                v.z = w.z * (v.z * inv);
+                v.w = w.w * (v.w * inv);
+                xv[m][j] = v;
+                if (a.xout != nullptr && blockIdx.x == 0)
+                    reinterpret_cast<float4*>(a.xout + (size_t)m * a.K)[k4] = v;
+            }
+        }
+    }
+}
+
+template <int M, int KV4, int XM, int EM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
+    using S = GemvShape<M, KV4>;
+    constexpr int RC = S::RC;
+    constexpr int NV = S::NV;
+    __shared__ float red[2][GEMV_WARPS][NV];
+    __shared__ float nred[GEMV_WARPS * M];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x;
+    // SwiGLU rows come in (gate, up) pairs: split pairs, not rows.
+    const int unit = (EM == E_SWIGLU) ? 2 : 1;
+    const int NU = a.N / unit;
+    const int r0 = (int)((long long)blockIdx.x * NU / G) * unit;
+    const int r1 = (int)((long long)(blockIdx.x + 1) * NU / G) * unit;
+    const int K4 = a.K >> 2;
+
+    prefetch_share(a.pf, blockIdx.x, G);
+
+    // First chunk of weights is independent of predecessors: issue it before the wait.
+    float4 wv[RC][KV4];
+#pragma unroll
+    for (int rc = 0; rc < RC; ++rc) {
+        const int r = r0 + rc;
+        const float4* wr = reinterpret_cast<const float4*>(gemv_row(a, r < r1 ? r : r0));
+#pragma unroll
+        for (int j = 0; j < KV4; ++j) {
+            const int k4 = tid + j * GEMV_THREADS;
+            wv[rc][j] = (r < r1 && k4 < K4) ? ldg_stream(wr + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+
+    pdl_wait();
+    pdl_trigger();
+    if (a.inc != nullptr && blockIdx.x == 0 && tid < a.n_inc) a.inc[tid] += 1;
+
+    float4 xv[M][KV4];
+    gemv_load_x<M, KV4, XM>(a, xv, nred);
+
+    int buf = 0;
+    for (int base = r0; base < r1; base += RC) {
+        float acc[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int rc = 0; rc < RC; ++rc) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float s = 0.f;
+#pragma unroll
+                for (int j = 0; j < KV4; ++j) {
+                    s = fmaf(wv[rc][j].x, xv[m][j].x, s);
+                    s = fmaf(wv[rc][j].y, xv[m][j].y, s);
+                    s = fmaf(wv[rc][j].z, xv[m][j].z, s);
+                    s = fmaf(wv[rc][j].w, xv[m][j].w, s);
+                }
+                acc[rc * M + m] = s;
+            }
+        }
+        // issue the next chunk's weight loads before reducing this one
+        const int nbase = base + RC;
+        if (nbase < r1) {
+#pragma unroll
+            for (int rc = 0; rc < RC; ++rc) {
+                const int r = nbase + rc;
+                const float4* wr = reinterpret_cast<const float4*>(gemv_row(a, r < r1 ? r : r0));
+#pragma unroll
+                for (int j = 0; j < KV4; ++j) {
+                    const int k4 = tid + j * GEMV_THREADS;
+                    wv[rc][j] = (r < r1 && k4 < K4) ? ldg_stream(wr + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        }
+        const float v = butterfly_reduce<NV>(acc, lane);
+        constexpr int DUP = 32 / NV;  // lanes holding each value
+        if ((lane & (DUP - 1)) == 0) red[buf][warp][lane / DUP] = v;
+        __syncthreads();
+        if (EM == E_SWIGLU) {
+            if (tid < (RC / 2) * M) {
+                const int p = tid / M, m = tid % M;
+                const int rg = base + 2 * p;
+                if (rg < r1) {
+                    float g = 0.f, u = 0.f;
+#pragma unroll
+                    for (int w = 0; w < GEMV_WARPS; ++w) {
+                        g += red[buf][w][(2 * p) * M + m];
+                        u += red[buf][w][(2 * p + 1) * M + m];
+                    }
+                    a.out[(size_t)m * a.ldo + (rg >> 1)] = silu(g) * u;
+                }
+            }
+        } else {
+            if (tid < RC * M) {
+                const int rc = tid / M, m = tid % M;
+                const int r = base + rc;
+                if (r < r1) {
+                    float s = 0.f;
+#pragma unroll
+                    for (int w = 0; w < GEMV_WARPS; ++w) s += red[buf][w][rc * M + m];
+                    if (EM == E_RESID) s += a.resid[(size_t)m * a.ldr + r];
+                    if (EM == E_BIAS) s += __ldg(a.bias + r);
+                    a.out[(size_t)m * a.ldo + r] = s;
+                }
+            }
+        }
+        buf ^= 1;
+    }
+}
+
+// Host-side dispatch over (M, KV4, XM, EM).  Returns a cudaError_t.
+cudaError_t gemv_launch(const GemvArgs& a, int M, int XM, int EM, int grid, cudaStream_t stream,
+                        bool pdl);
+
+}  // namespace skb

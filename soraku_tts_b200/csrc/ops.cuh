@@ -1,0 +1,24 @@
+// Internal declarations shared by the translation units of libsoraku_b200.so.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace skb {
+
+int fail(int code, const char* fmt, ...);
+int check_launch(const char* what);
+bool aligned16(const void* p);
+
+int rmsnorm_rows(const float* x, const float* x2, const float* w, float* out, int B, int D,
+                 float eps, cudaStream_t s, bool pdl);
+int cfg_sample(const float* logits, int rows_per_req, int n_req, int V,
+               const skb_sample_params* params, int bos, int pad, int eos, int64_t* codes,
+               float* uniforms, cudaStream_t s, bool pdl);
+GemvArgs gemv_args_plain(const float* x, int ldx, int N, int K);
+
+cudaError_t gemv_launch_m1(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
+cudaError_t gemv_launch_m2(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
+cudaError_t gemv_launch_m4(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
+
+}  // namespace skb

@@ -1,0 +1,356 @@
+// Fused CFG + mask + temperature + top-k + top-p + draw for one request, run
+// by one 256-thread CTA.  Restates soraku_inference/model.py:579-595 and
+// _sample_logits (model.py:686-708) with an explicit Philox uniform in place
+// of torch.multinomial:
+//
+//   merged = u + s * (c - u)                     (model.py:581; IEEE ops, no FMA)
+//   BOS, PAD (and EOS when masked) -> -inf        (model.py:582-584)
+//   temperature <= 0 -> first maximal index       (model.py:694-695)
+//   f = merged / temperature (+0.0 folds -0 into +0)
+//   top-k: cutoff = k-th largest f (duplicates counted); keep f >= cutoff
+//   candidates ordered by (f descending, index ascending)
+//   e_j = exp(f_j - f_0) with the exp below
+//   top-p: S1 = sequential sum of e_j; cum = sequential sum of e_j / S1;
+//          keep the prefix up to and including the first j with cum > p
+//   draw: S2 = sequential sum of kept e_j; first kept j whose sequential
+//         running sum of e_j exceeds u * S2 (else the last kept j with e_j > 0)
+//
+// Every float operation below rounds once, in the order written (explicit
+// __f*_rn intrinsics stop the compiler from contracting), so the result is
+// identical to the C restatement in the oracle for the same logits and u.
+//
+// Top-k selection: one 2048-bin histogram pass over the top 11 bits of an
+// order-preserving integer key of f finds the bin holding the k-th largest;
+// every element at or above that bin is compacted (typically ~k + a few
+// dozen) and rank-sorted exactly by (key, index).  With top-k off every
+// element is a candidate (slow path, O(V^2 / 256) compares).
+#pragma once
+
+#include "common.cuh"
+
+namespace skb {
+
+constexpr int SAMPLER_THREADS = 256;
+constexpr int SAMPLER_VMAX = 4096;
+constexpr int SAMPLER_BINS = 2048;
+
+// Dynamic shared memory layout of the sampler (bytes).
+constexpr size_t SAMPLER_SMEM = (size_t)SAMPLER_VMAX * 8  // f (floats), then sorted keys (u64)
+                                + (size_t)SAMPLER_VMAX * 8  // candidates (u64), then e (floats)
+                                + SAMPLER_BINS * 4          // histogram
+                                + 256;                      // scalars
+
+// ---------------------------------------------------------------- exp
+// Cody-Waite reduction + degree-7 Taylor polynomial (W. J. Cody and W. Waite,
+// "Software Manual for the Elementary Functions", 1980); results below 2^-126
+// flush to zero.  Same operations as orc_exp in the oracle.
+__device__ __forceinline__ float skb_exp(float x) {
+    const float LOG2E = 1.44269502162933349609375f;
+    const float LN2_HI = 0.693145751953125f;
+    const float LN2_LO = 1.428606765330187045e-06f;
+    if (x != x) return x;
+    if (x == -INFINITY) return 0.0f;
+    if (x < -104.0f) return 0.0f;
+    if (x > 88.7f) return INFINITY;
+    const float t = __fmul_rn(x, LOG2E);
+    const float n = rintf(t);
+    float r = __fmaf_rn(-n, LN2_HI, x);
+    r = __fmaf_rn(-n, LN2_LO, r);
+    float p = 1.984126984126984e-04f;
+    p = __fmaf_rn(p, r, 1.388888888888889e-03f);
+    p = __fmaf_rn(p, r, 8.333333333333333e-03f);
+    p = __fmaf_rn(p, r, 4.166666666666667e-02f);
+    p = __fmaf_rn(p, r, 1.666666666666667e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = (int)n;
+    if (ni < -126) return 0.0f;
+    if (ni > 127) return INFINITY;
+    const float scale = __int_as_float((ni + 127) << 23);
+    const float y = __fmul_rn(p, scale);
+    if (y < 1.17549435e-38f) return 0.0f;
+    return y;
+}
+
+// -------------------------------------------------------------- philox
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11).
+__device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int round = 0; round < 10; ++round) {
+        if (round > 0) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        const uint32_t lo0 = 0xD2511F53u * c[0];
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c[0]);
+        const uint32_t lo1 = 0xCD9E8D57u * c[2];
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]);
+        const uint32_t n0 = hi1 ^ c[1] ^ k0;
+        const uint32_t n2 = hi0 ^ c[3] ^ k1;
+        c[0] = n0;
+        c[1] = lo1;
+        c[2] = n2;
+        c[3] = lo0;
+    }
+}
+
+__device__ __forceinline__ float philox_uniform(uint64_t seed, uint32_t request, uint32_t frame,
+                                                uint32_t q) {
+    uint32_t c[4] = {q, frame, request, 0u};
+    philox4x32_10(c, (uint32_t)(seed & 0xffffffffu), (uint32_t)(seed >> 32));
+    return __fmul_rn((float)(c[0] >> 8), 1.0f / 16777216.0f);
+}
+
+// Order-preserving key: a < b (as floats, no NaN) <=> key(a) < key(b).
+__device__ __forceinline__ uint32_t ord_key(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+struct SampleJob {
+    const float* cond;    // [V]
+    const float* uncond;  // [V] or nullptr
+    int V;
+    float cfg_scale, temperature, top_p;
+    int top_k, mask_eos, bos, pad, eos;
+    float u;
+};
+
+// Block-wide exclusive scan of one int per thread (256 threads).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* tmp /* [8] */, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(FULL, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) tmp[warp] = x;
+    __syncthreads();
+    int wprefix = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        const int t = tmp[w];
+        if (w < warp) wprefix += t;
+        tot += t;
+    }
+    __syncthreads();
+    *total = tot;
+    return wprefix + x - v;
+}
+
+// Returns the drawn code (same value in every thread).  smem: SAMPLER_SMEM
+// bytes of dynamic shared memory, 16-byte aligned.  Requires V <= SAMPLER_VMAX.
+static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n_kept_out = nullptr) {
+    float* f = reinterpret_cast<float*>(smem);
+    unsigned long long* sorted = reinterpret_cast<unsigned long long*>(smem);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem + (size_t)SAMPLER_VMAX * 8);
+    float* e = reinterpret_cast<float*>(smem + (size_t)SAMPLER_VMAX * 8);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + (size_t)SAMPLER_VMAX * 16);
+    int* sc = reinterpret_cast<int*>(smem + (size_t)SAMPLER_VMAX * 16 + SAMPLER_BINS * 4);
+    // sc[0..7] scan tmp, sc[8] count, sc[9] bin, sc[10] n_keep_topk, sc[11] keep, sc[12] pick,
+    // sc[16..] reduction scratch
+    float* scf = reinterpret_cast<float*>(sc + 16);
+
+    const int tid = threadIdx.x;
+    const int V = J.V;
+    const bool greedy = !(J.temperature > 0.0f);
+
+    for (int i = tid; i < V; i += SAMPLER_THREADS) {
+        float c = __ldcg(J.cond + i);
+        float m;
+        if (J.uncond != nullptr) {
+            const float un = __ldcg(J.uncond + i);
+            m = __fadd_rn(un, __fmul_rn(J.cfg_scale, __fsub_rn(c, un)));
+        } else {
+            m = c;
+        }
+        if (i == J.bos || i == J.pad || (J.mask_eos && i == J.eos)) m = -INFINITY;
+        if (!greedy) m = __fadd_rn(__fdiv_rn(m, J.temperature), 0.0f);
+        f[i] = m;
+    }
+    __syncthreads();
+
+    if (greedy) {
+        // first maximal index
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int i = tid; i < V; i += SAMPLER_THREADS) {
+            const float v = f[i];
+            if (v > bv || (v == bv && i < bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(FULL, bv, o);
+            const int oi = __shfl_xor_sync(FULL, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((tid & 31) == 0) {
+            scf[tid >> 5] = bv;
+            sc[8 + (tid >> 5) + 16] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float b = scf[0];
+            int idx = sc[8 + 16];
+            for (int w = 1; w < 8; ++w) {
+                const float v = scf[w];
+                const int ii = sc[8 + w + 16];
+                if (v > b || (v == b && ii < idx)) {
+                    b = v;
+                    idx = ii;
+                }
+            }
+            sc[12] = idx;
+            sc[11] = 1;
+        }
+        __syncthreads();
+        if (n_kept_out) *n_kept_out = 1;
+        const int code = sc[12];
+        __syncthreads();
+        return code;
+    }
+
+    const bool topk_on = J.top_k > 0 && J.top_k < V;
+    uint32_t low_key = 0;
+    if (topk_on) {
+        for (int b = tid; b < SAMPLER_BINS; b += SAMPLER_THREADS) hist[b] = 0;
+        __syncthreads();
+        for (int i = tid; i < V; i += SAMPLER_THREADS) atomicAdd(&hist[ord_key(f[i]) >> 21], 1u);
+        __syncthreads();
+        // thread t owns descending bins 2047-8t .. 2040-8t
+        int s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += (int)hist[SAMPLER_BINS - 1 - (tid * 8 + j)];
+        int total;
+        const int before = block_exclusive_scan(s, sc, &total);
+        if (before < J.top_k && J.top_k <= before + s) {
+            int acc = before;
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+                const int b = SAMPLER_BINS - 1 - (tid * 8 + j);
+                const int h = (int)hist[b];
+                if (acc + h >= J.top_k) {
+                    sc[9] = b;
+                    break;
+                }
+                acc += h;
+            }
+        }
+        __syncthreads();
+        low_key = (uint32_t)sc[9] << 21;
+    }
+    if (tid == 0) sc[8] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += SAMPLER_THREADS) {
+        const uint32_t k = ord_key(f[i]);
+        if (k >= low_key) {
+            const int slot = atomicAdd(&sc[8], 1);
+            cand[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+        }
+    }
+    __syncthreads();
+    const int C = sc[8];
+    // exact rank sort, descending by (key, -index)
+    for (int i = tid; i < C; i += SAMPLER_THREADS) {
+        const unsigned long long ki = cand[i];
+        int rank = 0;
+        for (int j = 0; j < C; ++j) rank += (cand[j] > ki) ? 1 : 0;
+        sorted[rank] = ki;
+    }
+    __syncthreads();
+    // top-k: keep the sorted prefix with f >= cutoff (ties kept)
+    int n = C;
+    if (topk_on) {
+        const float cutoff = key_float((uint32_t)(sorted[J.top_k - 1] >> 32));
+        int cnt = 0;
+        for (int i = tid; i < C; i += SAMPLER_THREADS)
+            cnt += (key_float((uint32_t)(sorted[i] >> 32)) < cutoff) ? 0 : 1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
+        if ((tid & 31) == 0) sc[16 + (tid >> 5)] = cnt;
+        __syncthreads();
+        if (tid == 0) {
+            int t = 0;
+            for (int w = 0; w < 8; ++w) t += sc[16 + w];
+            sc[10] = t;
+        }
+        __syncthreads();
+        n = sc[10];
+    }
+    const float top = key_float((uint32_t)(sorted[0] >> 32));
+    for (int j = tid; j < n; j += SAMPLER_THREADS)
+        e[j] = skb_exp(__fsub_rn(key_float((uint32_t)(sorted[j] >> 32)), top));
+    __syncthreads();
+    // sequential FP32 sums in candidate order (thread 0), as the oracle does
+    const bool topp_on = J.top_p > 0.0f && J.top_p < 1.0f;
+    if (topp_on) {
+        if (tid == 0) {
+            float s1 = 0.0f;
+            for (int j = 0; j < n; ++j) s1 = __fadd_rn(s1, e[j]);
+            scf[0] = s1;
+        }
+        __syncthreads();
+        const float s1 = scf[0];
+        // e_j / S1 in parallel into the candidate area beyond e (floats)
+        float* pj = e + SAMPLER_VMAX;
+        for (int j = tid; j < n; j += SAMPLER_THREADS) pj[j] = __fdiv_rn(e[j], s1);
+        __syncthreads();
+        if (tid == 0) {
+            int keep = n;
+            float cum = 0.0f;
+            for (int j = 0; j < n; ++j) {
+                cum = __fadd_rn(cum, pj[j]);
+                if (cum > J.top_p) {
+                    keep = j + 1;
+                    break;
+                }
+            }
+            sc[11] = keep;
+        }
+    } else if (tid == 0) {
+        sc[11] = n;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const int keep = sc[11];
+        float s2 = 0.0f;
+        for (int j = 0; j < keep; ++j) s2 = __fadd_rn(s2, e[j]);
+        const float t = __fmul_rn(J.u, s2);
+        int pick = -1;
+        float run = 0.0f;
+        for (int j = 0; j < keep; ++j) {
+            run = __fadd_rn(run, e[j]);
+            if (run > t) {
+                pick = j;
+                break;
+            }
+        }
+        if (pick < 0) {
+            pick = 0;
+            for (int j = keep - 1; j >= 0; --j)
+                if (e[j] > 0.0f) {
+                    pick = j;
+                    break;
+                }
+        }
+        sc[12] = (int)(0xffffffffu - (uint32_t)(sorted[pick] & 0xffffffffull));
+    }
+    __syncthreads();
+    if (n_kept_out) *n_kept_out = sc[11];
+    const int code = sc[12];
+    __syncthreads();
+    return code;
+}
+
+}  // namespace skb

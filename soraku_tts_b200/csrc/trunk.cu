@@ -1,0 +1,535 @@
+// Trunk kernels: decode attention (split over the KV positions, last-CTA
+// combine) and the prefill path (embedding, SIMT FP32 GEMM, q/k norm + RoPE +
+// KV write, causal attention).
+#include "ops.cuh"
+#include "trunk.cuh"
+#include "trunk_api.cuh"
+
+namespace skb {
+
+// q/k RMSNorm over one head (hd = 128, 4 elements per lane) then neox RoPE.
+// Lane l holds elements [4l, 4l+4); its RoPE partner elements (+-64) live in
+// lane l ^ 16.
+__device__ __forceinline__ float4 norm_rope_head(float4 x, const float* w, float eps,
+                                                 const float* cosr, const float* sinr, int lane,
+                                                 bool do_norm, bool do_rope) {
+    if (do_norm) {
+        float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / 128.0f + eps);
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + lane);
+        x.x = wv.x * (x.x * inv);
+        x.y = wv.y * (x.y * inv);
+        x.z = wv.z * (x.z * inv);
+        x.w = wv.w * (x.w * inv);
+    }
+    if (do_rope) {
+        float4 o;
+        o.x = __shfl_xor_sync(FULL, x.x, 16);
+        o.y = __shfl_xor_sync(FULL, x.y, 16);
+        o.z = __shfl_xor_sync(FULL, x.z, 16);
+        o.w = __shfl_xor_sync(FULL, x.w, 16);
+        const int i0 = (lane & 15) * 4;  // frequency index of element 0
+        const float4 c = *reinterpret_cast<const float4*>(cosr + i0);
+        const float4 s = *reinterpret_cast<const float4*>(sinr + i0);
+        if (lane < 16) {  // first half: x*cos - x[i+64]*sin
+            x.x = x.x * c.x - o.x * s.x;
+            x.y = x.y * c.y - o.y * s.y;
+            x.z = x.z * c.z - o.z * s.z;
+            x.w = x.w * c.w - o.w * s.w;
+        } else {  // second half: x*cos + x[i-64]*sin
+            x.x = x.x * c.x + o.x * s.x;
+            x.y = x.y * c.y + o.y * s.y;
+            x.z = x.z * c.z + o.z * s.z;
+            x.w = x.w * c.w + o.w * s.w;
+        }
+    }
+    return x;
+}
+
+// grid (S, KVH, R), 256 threads, dynamic smem n_rep * nmax floats.
+__global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a) {
+    extern __shared__ float sc[];
+    __shared__ __align__(16) float qs[2][128];
+    __shared__ __align__(16) float ks[128];
+    __shared__ __align__(16) float vs[128];
+    __shared__ float sm_m[2], sm_l[2];
+    __shared__ int sm_last;
+
+    const int s = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nblk = gridDim.x * gridDim.y * gridDim.z;
+    prefetch_share(a.pf, (r * gridDim.y + g) * gridDim.x + s, nblk);
+    pdl_wait();
+    pdl_trigger();
+
+    int p_new = a.pos[r];
+    if (p_new < 0 || p_new >= a.max_len) {
+        if (tid == 0) atomicExch(a.err, 1);
+        p_new = p_new < 0 ? 0 : a.max_len - 1;
+    }
+    const int T = p_new + 1;
+    const float* row = a.qkv + (size_t)r * a.ld_qkv;
+    const float* cosr = a.rope_cos + (size_t)p_new * 64;
+    const float* sinr = a.rope_sin + (size_t)p_new * 64;
+    const int n_rep = a.n_rep;
+    if (warp == 0) {
+        float4 k = ld_cg4(reinterpret_cast<const float4*>(row + (a.H + g) * 128) + lane);
+        k = norm_rope_head(k, a.kn, a.eps, cosr, sinr, lane, true, true);
+        reinterpret_cast<float4*>(ks)[lane] = k;
+    } else if (warp <= n_rep) {
+        const int h = g * n_rep + (warp - 1);
+        float4 q = ld_cg4(reinterpret_cast<const float4*>(row + h * 128) + lane);
+        q = norm_rope_head(q, a.qn, a.eps, cosr, sinr, lane, true, true);
+        reinterpret_cast<float4*>(qs[warp - 1])[lane] = q;
+    } else if (warp == n_rep + 1) {
+        const float4 v =
+            ld_cg4(reinterpret_cast<const float4*>(row + (a.H + a.kv.KVH + g) * 128) + lane);
+        reinterpret_cast<float4*>(vs)[lane] = v;
+    }
+    __syncthreads();
+
+    const int pb = (int)((long long)s * T / a.S);
+    const int pe = (int)((long long)(s + 1) * T / a.S);
+    const int n = pe - pb;
+    if (s == a.S - 1 && tid < 128) {
+        a.kv.at(a.layer, r, p_new, 0, g)[tid] = ks[tid];
+        a.kv.at(a.layer, r, p_new, 1, g)[tid] = vs[tid];
+    }
+    // scores: one warp per position
+    for (int p = pb + warp; p < pe; p += 8) {
+        float4 k4;
+        if (p == p_new)
+            k4 = reinterpret_cast<const float4*>(ks)[lane];
+        else
+            k4 = ld_cg4(reinterpret_cast<const float4*>(a.kv.at(a.layer, r, p, 0, g)) + lane);
+        for (int h = 0; h < n_rep; ++h) {
+            const float4 q4 = reinterpret_cast<const float4*>(qs[h])[lane];
+            float d = q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w;
+            d = warp_sum(d);
+            if (lane == 0) sc[h * a.nmax + (p - pb)] = d * a.scale;
+        }
+    }
+    __syncthreads();
+    if (warp < n_rep) {
+        float* sh = sc + warp * a.nmax;
+        float m = -INFINITY;
+        for (int i = lane; i < n; i += 32) m = fmaxf(m, sh[i]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int i = lane; i < n; i += 32) {
+            const float e = (n > 0) ? expf(sh[i] - m) : 0.f;
+            sh[i] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            sm_m[warp] = m;
+            sm_l[warp] = l;
+        }
+    }
+    __syncthreads();
+    const int hd2 = 128 + 2;
+    float* part = a.part + ((((size_t)r * a.kv.KVH + g) * a.S + s) * n_rep) * hd2;
+    if (tid < n_rep * 128) {
+        const int h = tid >> 7, d = tid & 127;
+        const float* sh = sc + h * a.nmax;
+        float o = 0.f;
+        int i = 0;
+        for (; i + 4 <= n; i += 4) {
+            float v0, v1, v2, v3;
+            const int p0 = pb + i;
+            v0 = (p0 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0, 1, g) + d);
+            v1 = (p0 + 1 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0 + 1, 1, g) + d);
+            v2 = (p0 + 2 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0 + 2, 1, g) + d);
+            v3 = (p0 + 3 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0 + 3, 1, g) + d);
+            o = fmaf(sh[i], v0, o);
+            o = fmaf(sh[i + 1], v1, o);
+            o = fmaf(sh[i + 2], v2, o);
+            o = fmaf(sh[i + 3], v3, o);
+        }
+        for (; i < n; ++i) {
+            const int p = pb + i;
+            const float v = (p == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p, 1, g) + d);
+            o = fmaf(sh[i], v, o);
+        }
+        part[h * hd2 + d] = o;
+        if (d == 0) {
+            part[h * hd2 + 128] = sm_m[h];
+            part[h * hd2 + 129] = sm_l[h];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sm_last = (atomicAdd(&a.counters[r * a.kv.KVH + g], 1) == a.S - 1) ? 1 : 0;
+    __syncthreads();
+    if (!sm_last) return;
+    __threadfence();
+    if (tid < n_rep * 128) {
+        const int h = tid >> 7, d = tid & 127;
+        const float* base = a.part + ((((size_t)r * a.kv.KVH + g) * a.S) * n_rep) * hd2;
+        float M = -INFINITY;
+        for (int j = 0; j < a.S; ++j) M = fmaxf(M, __ldcg(base + ((size_t)j * n_rep + h) * hd2 + 128));
+        float L = 0.f, O = 0.f;
+        for (int j = 0; j < a.S; ++j) {
+            const float* pj = base + ((size_t)j * n_rep + h) * hd2;
+            const float w = expf(__ldcg(pj + 128) - M);
+            L = fmaf(__ldcg(pj + 129), w, L);
+            O = fmaf(__ldcg(pj + d), w, O);
+        }
+        a.out[(size_t)r * a.H * 128 + (g * n_rep + h) * 128 + d] = O / L;
+    }
+    if (tid == 0) a.counters[r * a.kv.KVH + g] = 0;
+}
+
+cudaError_t decode_attn_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl) {
+    const size_t smem = (size_t)a.n_rep * a.nmax * sizeof(float);
+    return launch(decode_attn_kernel, dim3(a.S, a.kv.KVH, R), dim3(256), smem, s, pdl, a);
+}
+
+// ------------------------------------------------------------------ prefill
+// Token embeddings (model.py:623-653): text ids through the text table with
+// language-id substitution (embed_text, model.py:326-338); audio frames as
+// scale * sum_q table[q, code]; the speaker slot vector.
+__global__ void __launch_bounds__(256) prefill_embed_kernel(
+    const PrefillTok* __restrict__ toks, const float* __restrict__ embed, int text_vocab,
+    const float* __restrict__ lang, int n_lang, int4 lang_ids, const int64_t* __restrict__ frames,
+    int Q, const float* __restrict__ table, int V, float scale, const float* __restrict__ slot,
+    const float* __restrict__ bos_add, float* __restrict__ X, int D, int* err) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    const PrefillTok tk = toks[t];
+    float* xo = X + (size_t)t * D;
+    if (tk.kind == 0) {
+        int id = tk.val;
+        int li = -1;
+        if (n_lang == 4) {
+            if (id == lang_ids.x) li = 0;
+            else if (id == lang_ids.y) li = 1;
+            else if (id == lang_ids.z) li = 2;
+            else if (id == lang_ids.w) li = 3;
+        }
+        if (li < 0 && (id < 0 || id >= text_vocab)) {
+            if (threadIdx.x == 0) atomicExch(err, 2);
+            id = 0;
+        }
+        const float* src = li >= 0 ? lang + (size_t)li * D : embed + (size_t)id * D;
+        for (int i = threadIdx.x; i < D; i += 256) xo[i] = src[i];
+    } else if (tk.kind == 1) {
+        const int64_t* fc = frames + (size_t)tk.val * Q;
+        for (int i = threadIdx.x; i < D; i += 256) {
+            float acc = 0.f;
+            for (int q = 0; q < Q; ++q) {
+                long long c = fc[q];
+                if (c < 0 || c >= V) {
+                    atomicExch(err, 3);
+                    c = 0;
+                }
+                const float v = table[((size_t)q * V + (size_t)c) * D + i];
+                acc = (q == 0) ? v : acc + v;
+            }
+            acc = acc * scale;
+            if (bos_add != nullptr && tk.val == 0) acc = acc + bos_add[i];
+            xo[i] = acc;
+        }
+    } else {
+        for (int i = threadIdx.x; i < D; i += 256) xo[i] = slot[i];
+    }
+}
+
+// Speaker projection (model.py:404-421): out = W @ normalize(v) (+ slot), 1 CTA.
+__global__ void __launch_bounds__(256) speaker_kernel(const float* __restrict__ v, int SD,
+                                                      const float* __restrict__ W, int D,
+                                                      const float* __restrict__ slot_emb,
+                                                      float* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float vs[1024];
+    __shared__ float red[8];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < SD; i += 256) {
+        const float x = v[i];
+        vs[i] = x;
+        ss += x * x;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float nrm = fmaxf(sqrtf(tot), 1e-12f);
+    for (int i = threadIdx.x; i < SD; i += 256) vs[i] = vs[i] / nrm;
+    __syncthreads();
+    for (int o = threadIdx.x; o < D; o += 256) {
+        const float* wr = W + (size_t)o * SD;
+        float acc = 0.f;
+        for (int i = 0; i < SD; ++i) acc = fmaf(wr[i], vs[i], acc);
+        out[o] = slot_emb ? acc + slot_emb[o] : acc;
+    }
+}
+
+// C[t][n] = sum_k A[t][k] W(n)[k], 64x64 tiles, BK 16, 4x4 per thread.
+__device__ __forceinline__ const float* gemm_row(const GemmArgs& a, int n) {
+    if (a.interleave) return ((n & 1) ? a.w1 : a.w0) + (size_t)(n >> 1) * a.K;
+    if (n < a.seg1) return a.w0 + (size_t)n * a.K;
+    if (n < a.seg2) return a.w1 + (size_t)(n - a.seg1) * a.K;
+    return a.w2 + (size_t)(n - a.seg2) * a.K;
+}
+
+__global__ void __launch_bounds__(256) sgemm_kernel(const GemmArgs a) {
+    __shared__ __align__(16) float As[16][64 + 4];
+    __shared__ __align__(16) float Ws[16][64 + 4];
+    pdl_wait();
+    pdl_trigger();
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int n0 = blockIdx.x * 64, t0 = blockIdx.y * 64;
+    const int lr = tid >> 2, lk = (tid & 3) * 4;  // loader: row lr, k offset lk
+    const int tA = t0 + lr, nW = n0 + lr;
+    const float* arow = (tA < a.T) ? a.A + (size_t)tA * a.lda : nullptr;
+    const float* wrow = (nW < a.N) ? gemm_row(a, nW) : nullptr;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < a.K; k0 += 16) {
+        const float4 av = arow ? *reinterpret_cast<const float4*>(arow + k0 + lk) : make_float4(0, 0, 0, 0);
+        const float4 wv = wrow ? __ldg(reinterpret_cast<const float4*>(wrow + k0 + lk)) : make_float4(0, 0, 0, 0);
+        As[lk + 0][lr] = av.x;
+        As[lk + 1][lr] = av.y;
+        As[lk + 2][lr] = av.z;
+        As[lk + 3][lr] = av.w;
+        Ws[lk + 0][lr] = wv.x;
+        Ws[lk + 1][lr] = wv.y;
+        Ws[lk + 2][lr] = wv.z;
+        Ws[lk + 3][lr] = wv.w;
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const float4 x = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
+            const float4 w = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
+            const float xa[4] = {x.x, x.y, x.z, x.w};
+            const float wa[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + ty * 4 + i;
+        if (t >= a.T) continue;
+        if (a.mode == 3) {
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {
+                const int n = n0 + tx * 4 + j;
+                if (n + 1 < a.N) a.out[(size_t)t * a.ldo + (n >> 1)] = silu(acc[i][j]) * acc[i][j + 1];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + tx * 4 + j;
+                if (n >= a.N) continue;
+                float v = acc[i][j];
+                if (a.mode == 1) v += a.resid[(size_t)t * a.ldr + n];
+                a.out[(size_t)t * a.ldo + n] = v;
+            }
+        }
+    }
+}
+
+cudaError_t sgemm_launch(const GemmArgs& a, cudaStream_t s) {
+    if (a.K % 16 != 0) return cudaErrorInvalidValue;
+    return launch(sgemm_kernel, dim3((a.N + 63) / 64, (a.T + 63) / 64), dim3(256), 0, s, false, a);
+}
+
+// Per token: q/k RMSNorm + RoPE at the token's position; q -> Qo, k/v -> KV.
+// grid T, 256 threads (warp w handles head vectors w, w+8, ...).
+__global__ void __launch_bounds__(256) prefill_qk_kernel(const float* __restrict__ qkv, int ld,
+                                                         const PrefillTok* __restrict__ toks,
+                                                         const float* qn, const float* kn, float eps,
+                                                         const float* rope_cos, const float* rope_sin,
+                                                         int H, KVLayout kv, int layer,
+                                                         float* __restrict__ Qo) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const PrefillTok tk = toks[t];
+    const float* row = qkv + (size_t)t * ld;
+    const float* cosr = rope_cos + (size_t)tk.pos * 64;
+    const float* sinr = rope_sin + (size_t)tk.pos * 64;
+    const int nvec = H + 2 * kv.KVH;
+    for (int v = warp; v < nvec; v += 8) {
+        float4 x = reinterpret_cast<const float4*>(row + v * 128)[lane];
+        if (v < H) {
+            x = norm_rope_head(x, qn, eps, cosr, sinr, lane, true, true);
+            reinterpret_cast<float4*>(Qo + (size_t)t * H * 128 + v * 128)[lane] = x;
+        } else if (v < H + kv.KVH) {
+            x = norm_rope_head(x, kn, eps, cosr, sinr, lane, true, true);
+            reinterpret_cast<float4*>(kv.at(layer, tk.row, tk.pos, 0, v - H))[lane] = x;
+        } else {
+            reinterpret_cast<float4*>(kv.at(layer, tk.row, tk.pos, 1, v - H - kv.KVH))[lane] = x;
+        }
+    }
+}
+
+// Causal attention of a row's prompt: grid (ceil(L/32), KVH, n_rows); each
+// CTA serves 32 query positions x n_rep heads = 64 query vectors (8 per warp,
+// staged pre-scaled in shared memory); keys and values stream through shared
+// memory 32 positions at a time with an online softmax.
+constexpr int PATTN_SMEM = (64 * 128 + 32 * 129 + 32 * 128) * 4;
+
+__global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ Q,
+                                                           const int* __restrict__ row_off,
+                                                           const int* __restrict__ row_len,
+                                                           const int* __restrict__ row_id,
+                                                           int H, int n_rep, KVLayout kv, int layer,
+                                                           float scale, float* __restrict__ out) {
+    extern __shared__ float psm[];
+    float* Qs = psm;                  // [64][128]
+    float* Ks = psm + 64 * 128;       // [32][129]
+    float* Vs = Ks + 32 * 129;        // [32][128]
+    pdl_wait();
+    pdl_trigger();
+    const int qb = blockIdx.x, g = blockIdx.y, ri = blockIdx.z;
+    const int L = row_len[ri], off = row_off[ri], row = row_id[ri];
+    const int q0 = qb * 32;
+    if (q0 >= L) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int QV = 8;
+    // query vector v: position q0 + v / n_rep, head g * n_rep + v % n_rep
+    for (int i = threadIdx.x; i < 64 * 128; i += 256) {
+        const int v = i >> 7, d = i & 127;
+        const int p = q0 + v / n_rep, h = g * n_rep + v % n_rep;
+        Qs[i] = (p < L && v < 32 * n_rep) ? Q[(size_t)(off + p) * H * 128 + h * 128 + d] * scale : 0.f;
+    }
+    float m[QV], l[QV], o[QV][4];
+    int qpos[QV];
+#pragma unroll
+    for (int j = 0; j < QV; ++j) {
+        const int v = warp * QV + j;
+        qpos[j] = (v < 32 * n_rep) ? q0 + v / n_rep : 0x7fffffff;
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
+    }
+    const int last_q = min(L - 1, q0 + 31);
+    for (int k0 = 0; k0 <= last_q; k0 += 32) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * 128; i += 256) {
+            const int kk = i >> 7, d = i & 127;
+            const int p = k0 + kk;
+            float kk_v = 0.f, vv = 0.f;
+            if (p < L) {
+                kk_v = kv.at(layer, row, p, 0, g)[d];
+                vv = kv.at(layer, row, p, 1, g)[d];
+            }
+            Ks[kk * 129 + d] = kk_v;
+            Vs[kk * 128 + d] = vv;
+        }
+        __syncthreads();
+        const int p = k0 + lane;
+        float sdot[QV];
+#pragma unroll
+        for (int j = 0; j < QV; ++j) sdot[j] = 0.f;
+        const float* qw = Qs + (warp * QV) * 128;
+#pragma unroll 4
+        for (int d = 0; d < 128; ++d) {
+            const float kd = Ks[lane * 129 + d];
+#pragma unroll
+            for (int j = 0; j < QV; ++j) sdot[j] = fmaf(qw[j * 128 + d], kd, sdot[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < QV; ++j) {
+            const bool valid = p <= qpos[j] && p < L && qpos[j] < L;
+            const float sv = valid ? sdot[j] : -INFINITY;
+            const float mt = warp_max(sv);
+            const float mn = fmaxf(m[j], mt);
+            if (mn == -INFINITY) continue;
+            const float pe = valid ? expf(sv - mn) : 0.f;
+            const float corr = expf(m[j] - mn);
+            l[j] = l[j] * corr + warp_sum(pe);
+            m[j] = mn;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[j][c] *= corr;
+            for (int kk = 0; kk < 32; ++kk) {
+                const float pk = __shfl_sync(FULL, pe, kk);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) o[j][c] = fmaf(pk, Vs[kk * 128 + lane + 32 * c], o[j][c]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < QV; ++j) {
+        if (qpos[j] >= L) continue;
+        const int v = warp * QV + j;
+        const int h = g * n_rep + v % n_rep;
+        const float inv = 1.0f / l[j];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            out[(size_t)(off + qpos[j]) * H * 128 + h * 128 + lane + 32 * c] = o[j][c] * inv;
+    }
+}
+
+// x_trunk[row] = X[last token of row]
+__global__ void gather_rows_kernel(const float* __restrict__ X, const int* __restrict__ src,
+                                   const int* __restrict__ dst, float* __restrict__ out, int D) {
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.x;
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        out[(size_t)dst[r] * D + i] = X[(size_t)src[r] * D + i];
+}
+
+cudaError_t prefill_embed_launch(const PrefillTok* toks, int T, const float* embed, int text_vocab,
+                                 const float* lang, int n_lang, const int* lang_ids,
+                                 const int64_t* frames, int Q, const float* table, int V,
+                                 float scale, const float* slot, const float* bos_add, float* X,
+                                 int D, int* err, cudaStream_t s) {
+    const int4 li = make_int4(lang_ids[0], lang_ids[1], lang_ids[2], lang_ids[3]);
+    return launch(prefill_embed_kernel, dim3(T), dim3(256), 0, s, false, toks, embed, text_vocab,
+                  lang, n_lang, li, frames, Q, table, V, scale, slot, bos_add, X, D, err);
+}
+
+cudaError_t speaker_launch(const float* v, int SD, const float* W, int D, const float* slot,
+                           float* out, cudaStream_t s) {
+    if (SD > 1024) return cudaErrorInvalidValue;
+    return launch(speaker_kernel, dim3(1), dim3(256), 0, s, false, v, SD, W, D, slot, out);
+}
+
+cudaError_t prefill_qk_launch(const float* qkv, int ld, const PrefillTok* toks, int T,
+                              const float* qn, const float* kn, float eps, const float* rc,
+                              const float* rs, int H, const KVLayout& kv, int layer, float* Qo,
+                              cudaStream_t s) {
+    return launch(prefill_qk_kernel, dim3(T), dim3(256), 0, s, false, qkv, ld, toks, qn, kn, eps, rc,
+                  rs, H, kv, layer, Qo);
+}
+
+cudaError_t prefill_attn_launch(const float* Q, const int* row_off, const int* row_len,
+                                const int* row_id, int n_rows, int max_L, int H, int n_rep,
+                                const KVLayout& kv, int layer, float scale, float* out,
+                                cudaStream_t s) {
+    if (n_rep < 1 || 32 * n_rep > 64) return cudaErrorInvalidValue;
+    return launch(prefill_attn_kernel, dim3((max_L + 31) / 32, kv.KVH, n_rows), dim3(256), PATTN_SMEM, s,
+                  false, Q, row_off, row_len, row_id, H, n_rep, kv, layer, scale, out);
+}
+
+cudaError_t trunk_init_attrs() {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PATTN_SMEM);
+    return e;
+}
+
+cudaError_t gather_rows_launch(const float* X, const int* src, const int* dst, int n, float* out,
+                               int D, cudaStream_t s) {
+    return launch(gather_rows_kernel, dim3(n), dim3(256), 0, s, false, X, src, dst, out, D);
+}
+
+}  // namespace skb
