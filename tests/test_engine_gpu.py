@@ -83,9 +83,9 @@ def _decode(model, data, n_frames, *, temperature=0.9, top_k=50, top_p=0.95, see
             eng.step_eager(1, True)
         torch.cuda.synchronize()
         logits.append(eng.view(4).view(model.config.num_codebooks, 2, -1).cpu().numpy().copy())
-    codes = eng.read_codes(0, 0, n_frames).clone().numpy()
+    codes = eng.read_codes(0, 0, n_frames).clone().numpy() if n_frames else np.zeros((0, 16), np.int64)
     eng.close()
-    return codes, np.stack(logits), hidden0
+    return codes, (np.stack(logits) if logits else None), hidden0
 
 
 def _check_frames(orc, data, meta, codes, logits, *, temperature, top_k, top_p, seed, speaker=None,
