@@ -185,6 +185,7 @@ struct WRange {
 // kernel's weights) and the weight ranges it reads.
 struct Node {
     std::vector<WRange> w;
+    int ctas = 0;  // CTAs of the launch; only wide kernels issue L2 prefetches
     std::function<cudaError_t(cudaStream_t, bool, const PrefetchList&)> run;
 };
 
@@ -207,8 +208,10 @@ std::vector<WRange> gemv_ranges(const GemvArgs& a) {
 Node gemv_node(const skb_engine* e, GemvArgs a, int M, int XM, int EM) {
     Node n;
     n.w = gemv_ranges(a);
+    a.err = e->err + 2;
     const int units = a.N / (EM == E_SWIGLU ? 2 : 1);
     const int grid = units < e->nsm ? units : e->nsm;
+    n.ctas = grid;
     n.run = [a, M, XM, EM, grid](cudaStream_t s, bool pdl, const PrefetchList& pf) {
         GemvArgs b = a;
         b.pf = pf;
@@ -281,6 +284,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.pad = e->m.pad_id;
             a.eos = e->m.eos_id;
             Node n;
+            n.ctas = n_active;
             n.run = [a, n_active](cudaStream_t s, bool pdl, const PrefetchList& pf) {
                 DepthSampleArgs b = a;
                 b.pf = pf;
@@ -327,6 +331,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.out = e->attn;
             a.err = e->err;
             Node n;
+            n.ctas = a.S * e->KVH * R;
             n.run = [a, R](cudaStream_t s, bool pdl, const PrefetchList& pf) {
                 DecodeAttnArgs b = a;
                 b.pf = pf;
@@ -382,12 +387,27 @@ PrefetchList make_pf(const std::vector<WRange>& w, bool on) {
     return pf;
 }
 
+// Prefetch policy: a kernel with at least 64 CTAs prefetches the weights of
+// the next kernel that reads weights, looking past one narrow, weightless
+// kernel (the sampler).  Narrow kernels never prefetch: one CTA issuing a
+// whole weight set is limited by its SM's request rate.
+PrefetchList prefetch_for(const skb_engine* e, const std::vector<Node>& nodes, size_t i) {
+    const size_t n = nodes.size();
+    if (!e->o.l2_prefetch || nodes[i].ctas < 64) return make_pf({}, false);
+    const Node& n1 = nodes[(i + 1) % n];
+    if (!n1.w.empty()) return make_pf(n1.w, true);
+    if (n1.ctas < 64) {
+        const Node& n2 = nodes[(i + 2) % n];
+        if (!n2.w.empty()) return make_pf(n2.w, true);
+    }
+    return make_pf({}, false);
+}
+
 int run_frames(skb_engine* e, const std::vector<Node>& nodes, int frames, cudaStream_t s, bool pdl) {
     const size_t n = nodes.size();
     for (int f = 0; f < frames; ++f) {
         for (size_t i = 0; i < n; ++i) {
-            const Node& nx = nodes[(i + 1) % n];
-            const PrefetchList pf = make_pf(nx.w, e->o.l2_prefetch != 0);
+            const PrefetchList pf = prefetch_for(e, nodes, i);
             const bool use_pdl = pdl && !(f == 0 && i == 0);
             cudaError_t err = nodes[i].run(s, use_pdl, pf);
             if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "frame kernel %zu: %s", i, cudaGetErrorString(err));
@@ -437,6 +457,15 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
         return fail(SKB_ERR_ARG, "engine_create: missing weight pointers");
     for (int i = 0; i < m.n_layers * SKB_LAYER_PTRS; ++i)
         if (!m.layers[i] || !aligned16(m.layers[i])) return fail(SKB_ERR_ARG, "layer weight %d null or unaligned", i);
+    {
+        const void* need[] = {m.embed_tokens, m.final_norm, m.table, m.depth_bias, m.depth_norm_in,
+                              m.depth_norm_out, m.depth_gate, m.depth_up, m.depth_down};
+        for (const void* p : need)
+            if (!p || !aligned16(p)) return fail(SKB_ERR_ARG, "engine weights must be non-null and 16-byte aligned");
+        const void* opt[] = {m.lang_embed, m.speaker_proj, m.speaker_slot};
+        for (const void* p : opt)
+            if (p && !aligned16(p)) return fail(SKB_ERR_ARG, "engine weights must be 16-byte aligned");
+    }
 
     skb_engine* e = new skb_engine();
     e->m = m;
@@ -463,12 +492,9 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     while ((1 << e->page_log2) < ps) ++e->page_log2;
     e->o.page_size = 1 << e->page_log2;
     e->max_pages = (opts->max_len + e->o.page_size - 1) / e->o.page_size;
-    e->S = opts->attn_splits > 0 ? opts->attn_splits : (e->nsm / (e->R * e->KVH) > 0 ? e->nsm / (e->R * e->KVH) : 1);
+    e->S = opts->attn_splits > 0 ? opts->attn_splits
+                                 : (2 * e->nsm / (e->R * e->KVH) > 0 ? 2 * e->nsm / (e->R * e->KVH) : 1);
     e->nmax = (opts->max_len + e->S - 1) / e->S + 1;
-    if ((size_t)e->n_rep * e->nmax * 4 > 160 * 1024) {
-        delete e;
-        return fail(SKB_ERR_ARG, "max_len %d too long for %d attention splits", opts->max_len, e->S);
-    }
     const size_t n_pages = (size_t)e->R * e->max_pages;
     e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;
     const int qkvd = (e->H + 2 * e->KVH) * e->hd;
@@ -551,6 +577,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     }
     cudaFuncSetAttribute(depth_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SAMPLER_SMEM);
     trunk_init_attrs();
+    gemv_prepare_all();
     const cudaError_t ce = cudaDeviceSynchronize();
     if (ce != cudaSuccess) {
         skb_engine_destroy(e);

@@ -3,13 +3,15 @@
 //
 // Layout on the GPU.  CTA c owns the contiguous output rows
 // [c*N/G, (c+1)*N/G) (G = grid), so its weight slice is one contiguous range
-// per weight segment and the CTAs' shares differ by at most one row.  Thread
-// t owns the K-slice of float4 columns {t, t+256, ...}: it keeps x[m, slice]
-// in registers for the whole kernel and streams W[n, slice] with 128-bit
-// loads, so each 256-thread pass reads one 4 KB weight row fully coalesced.
-// Rows are processed in chunks of RC; the RC*M partial dot products of a
-// chunk are reduced across the warp by a butterfly reduce-scatter and across
-// the 8 warps through shared memory.
+// per weight segment and the CTAs' shares differ by at most one row.  Before
+// waiting on its predecessor (programmatic dependent launch) thread 0 stages
+// the CTA's whole slice into shared memory with 1-D bulk copies (TMA engine),
+// one mbarrier per chunk of RC rows, so every weight byte of the kernel is in
+// flight at once.  Thread t owns the K-slice of float4 columns {t, t+256, ...}:
+// it keeps x[m, slice] in registers and reads W[n, slice] from shared memory
+// (conflict-free 128-bit loads).  The RC*M partial dot products of a chunk are
+// reduced across the warp by a butterfly reduce-scatter and across the 8 warps
+// through shared memory.
 //
 // Memory-bound: 4 bytes of weight per 2*M flops; no tensor cores (FP32
 // parity with the reference's native path is required).
@@ -64,6 +66,7 @@ struct GemvArgs {
     const float* bias;
     int* inc;   // optional: CTA 0 adds 1 to inc[0 .. n_inc) after the wait (position counters)
     int n_inc;
+    int* err;   // optional: set to 1 if a weight copy did not arrive
     PrefetchList pf;
 };
 
@@ -202,11 +205,19 @@ __device__ __forceinline__ void gemv_load_x(const GemvArgs& a, float4 (&xv)[M][K
     }
 }
 
+// Dynamic shared memory: [GEMV_MAX_CHUNKS mbarriers | pad to 256 B | weight rows].
+constexpr int GEMV_MAX_CHUNKS = 30;
+constexpr int GEMV_SMEM_HEAD = 256;
+constexpr size_t GEMV_SMEM_MAX = 220 * 1024;  // + ~2 KB static stays under the 227 KB opt-in limit
+
 template <int M, int KV4, int XM, int EM>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     using S = GemvShape<M, KV4>;
     constexpr int RC = S::RC;
     constexpr int NV = S::NV;
+    extern __shared__ __align__(128) unsigned char gsm[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(gsm);
+    float* wsm = reinterpret_cast<float*>(gsm + GEMV_SMEM_HEAD);
     __shared__ float red[2][GEMV_WARPS][NV];
     __shared__ float nred[GEMV_WARPS * M];
 
@@ -218,21 +229,32 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     const int r0 = (int)((long long)blockIdx.x * NU / G) * unit;
     const int r1 = (int)((long long)(blockIdx.x + 1) * NU / G) * unit;
     const int K4 = a.K >> 2;
-
-    prefetch_share(a.pf, blockIdx.x, G);
-
-    // First chunk of weights is independent of predecessors: issue it before the wait.
-    float4 wv[RC][KV4];
-#pragma unroll
-    for (int rc = 0; rc < RC; ++rc) {
-        const int r = r0 + rc;
-        const float4* wr = reinterpret_cast<const float4*>(gemv_row(a, r < r1 ? r : r0));
-#pragma unroll
-        for (int j = 0; j < KV4; ++j) {
-            const int k4 = tid + j * GEMV_THREADS;
-            wv[rc][j] = (r < r1 && k4 < K4) ? ldg_stream(wr + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    const int nrows = r1 - r0;
+    const int nch = (nrows + RC - 1) / RC;
+    const uint32_t row_bytes = (uint32_t)a.K * 4u;
+    if (nch > GEMV_MAX_CHUNKS) {  // the host sizes the grid so this never happens
+        if (tid == 0 && a.err) atomicExch(a.err, 2);
+        pdl_wait();
+        pdl_trigger();
+        return;
     }
+
+    // Everything up to the PDL wait touches only weights: stage this CTA's whole
+    // (contiguous) weight slice into shared memory with bulk copies, one
+    // mbarrier per chunk of RC rows, and prefetch the next kernel's share into L2.
+    if (tid == 0) {
+        for (int c = 0; c < nch; ++c) mbar_init(&bars[c], 1);
+        mbar_fence_init();
+        for (int c = 0; c < nch; ++c) {
+            const int rb = r0 + c * RC;
+            const int re = min(rb + RC, r1);
+            mbar_expect_tx(&bars[c], (uint32_t)(re - rb) * row_bytes);
+            for (int r = rb; r < re; ++r)
+                bulk_g2s(wsm + (size_t)(r - r0) * a.K, gemv_row(a, r), row_bytes, &bars[c]);
+        }
+        prefetch_share(a.pf, blockIdx.x, G);
+    }
+    __syncthreads();
 
     pdl_wait();
     pdl_trigger();
@@ -241,37 +263,35 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
     float4 xv[M][KV4];
     gemv_load_x<M, KV4, XM>(a, xv, nred);
 
+    bool ok = true;
     int buf = 0;
-    for (int base = r0; base < r1; base += RC) {
+    for (int c = 0; c < nch; ++c) {
+        const int base = r0 + c * RC;
+        if (ok) ok = mbar_wait(&bars[c], 0, a.err);
         float acc[NV];
 #pragma unroll
         for (int i = 0; i < NV; ++i) acc[i] = 0.f;
-#pragma unroll
-        for (int rc = 0; rc < RC; ++rc) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float s = 0.f;
-#pragma unroll
-                for (int j = 0; j < KV4; ++j) {
-                    s = fmaf(wv[rc][j].x, xv[m][j].x, s);
-                    s = fmaf(wv[rc][j].y, xv[m][j].y, s);
-                    s = fmaf(wv[rc][j].z, xv[m][j].z, s);
-                    s = fmaf(wv[rc][j].w, xv[m][j].w, s);
-                }
-                acc[rc * M + m] = s;
-            }
-        }
-        // issue the next chunk's weight loads before reducing this one
-        const int nbase = base + RC;
-        if (nbase < r1) {
+        if (ok) {
 #pragma unroll
             for (int rc = 0; rc < RC; ++rc) {
-                const int r = nbase + rc;
-                const float4* wr = reinterpret_cast<const float4*>(gemv_row(a, r < r1 ? r : r0));
+                if (base + rc < r1) {
+                    const float4* wr = reinterpret_cast<const float4*>(wsm + (size_t)(base + rc - r0) * a.K);
 #pragma unroll
-                for (int j = 0; j < KV4; ++j) {
-                    const int k4 = tid + j * GEMV_THREADS;
-                    wv[rc][j] = (r < r1 && k4 < K4) ? ldg_stream(wr + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int j = 0; j < KV4; ++j) {
+                        const int k4 = tid + j * GEMV_THREADS;
+                        if (k4 < K4) {
+                            const float4 w = wr[k4];
+#pragma unroll
+                            for (int m = 0; m < M; ++m) {
+                                float sacc = acc[rc * M + m];
+                                sacc = fmaf(w.x, xv[m][j].x, sacc);
+                                sacc = fmaf(w.y, xv[m][j].y, sacc);
+                                sacc = fmaf(w.z, xv[m][j].z, sacc);
+                                sacc = fmaf(w.w, xv[m][j].w, sacc);
+                                acc[rc * M + m] = sacc;
+                            }
+                        }
+                    }
                 }
             }
         }
@@ -298,21 +318,50 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
                 const int rc = tid / M, m = tid % M;
                 const int r = base + rc;
                 if (r < r1) {
-                    float s = 0.f;
+                    float sum = 0.f;
 #pragma unroll
-                    for (int w = 0; w < GEMV_WARPS; ++w) s += red[buf][w][rc * M + m];
-                    if (EM == E_RESID) s += a.resid[(size_t)m * a.ldr + r];
-                    if (EM == E_BIAS) s += __ldg(a.bias + r);
-                    a.out[(size_t)m * a.ldo + r] = s;
+                    for (int w = 0; w < GEMV_WARPS; ++w) sum += red[buf][w][rc * M + m];
+                    if (EM == E_RESID) sum += a.resid[(size_t)m * a.ldr + r];
+                    if (EM == E_BIAS) sum += __ldg(a.bias + r);
+                    a.out[(size_t)m * a.ldo + r] = sum;
                 }
             }
         }
         buf ^= 1;
     }
+    if (!ok) {
+        // a copy never arrived: wait (bounded) for every copy still in flight
+        // into this CTA's shared memory before the CTA exits
+        for (int c = 0; c < nch; ++c) mbar_wait(&bars[c], 0, nullptr);
+    }
 }
 
-// Host-side dispatch over (M, KV4, XM, EM).  Returns a cudaError_t.
+// Rows per CTA for N logical rows on G CTAs (pairs for SwiGLU).
+inline int gemv_rows_per_cta(int N, int EM, int G) {
+    const int unit = (EM == E_SWIGLU) ? 2 : 1;
+    const int NU = N / unit;
+    return ((NU + G - 1) / G) * unit;
+}
+inline size_t gemv_smem_bytes(int N, int K, int EM, int G) {
+    return GEMV_SMEM_HEAD + (size_t)gemv_rows_per_cta(N, EM, G) * K * 4;
+}
+// Smallest grid >= want whose per-CTA slice fits in shared memory and whose
+// chunk count fits the barrier array.
+inline int gemv_grid(int N, int K, int EM, int want, int rc) {
+    int G = want < 1 ? 1 : want;
+    for (;;) {
+        const int rows = gemv_rows_per_cta(N, EM, G);
+        if (gemv_smem_bytes(N, K, EM, G) <= GEMV_SMEM_MAX && (rows + rc - 1) / rc <= GEMV_MAX_CHUNKS) return G;
+        ++G;
+    }
+}
+
+// Host-side dispatch over (M, KV4, XM, EM).  `grid` is the wanted CTA count;
+// it grows if a CTA's slice would not fit in shared memory.  Returns a cudaError_t.
 cudaError_t gemv_launch(const GemvArgs& a, int M, int XM, int EM, int grid, cudaStream_t stream,
                         bool pdl);
+// Sets the dynamic shared-memory limit of every instantiation (call before
+// stream capture).
+cudaError_t gemv_prepare_all();
 
 }  // namespace skb

@@ -11,11 +11,19 @@
 
 namespace skb {
 
+template <int KV4, int XMV, int EMV>
+static cudaError_t gemv_go(const GemvArgs& a, int grid, cudaStream_t s, bool pdl) {
+    auto kern = gemv_kernel<GEMV_M, KV4, XMV, EMV>;
+    if (grid <= 0)  // prepare only
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_MAX);
+    const int G = gemv_grid(a.N, a.K, EMV, grid, GemvShape<GEMV_M, KV4>::RC);
+    return launch(kern, dim3(G), dim3(GEMV_THREADS), gemv_smem_bytes(a.N, a.K, EMV, G), s, pdl, a);
+}
+
 template <int KV4>
 static cudaError_t gemv_dispatch_em(const GemvArgs& a, int XM, int EM, int grid, cudaStream_t s, bool pdl) {
 #define SKB_CASE(XMV, EMV)                                                                       \
-    if (XM == XMV && EM == EMV)                                                                  \
-        return launch(gemv_kernel<GEMV_M, KV4, XMV, EMV>, dim3(grid), dim3(GEMV_THREADS), 0, s, pdl, a);
+    if (XM == XMV && EM == EMV) return gemv_go<KV4, XMV, EMV>(a, grid, s, pdl);
     SKB_CASE(X_PLAIN, E_STORE)
     SKB_CASE(X_PLAIN, E_RESID)
     SKB_CASE(X_PLAIN, E_BIAS)
@@ -27,6 +35,19 @@ static cudaError_t gemv_dispatch_em(const GemvArgs& a, int XM, int EM, int grid,
     SKB_CASE(X_NORM_ADD_NORM, E_SWIGLU)
 #undef SKB_CASE
     return cudaErrorInvalidValue;
+}
+
+cudaError_t SKB_CAT(gemv_prepare_m, GEMV_M)() {
+    GemvArgs a = {};
+    const int pairs[9][2] = {{X_PLAIN, E_STORE}, {X_PLAIN, E_RESID}, {X_PLAIN, E_BIAS}, {X_PLAIN, E_SWIGLU},
+                             {X_RMSNORM, E_STORE}, {X_RMSNORM, E_SWIGLU}, {X_RMSNORM, E_BIAS},
+                             {X_ADD_RMSNORM, E_SWIGLU}, {X_NORM_ADD_NORM, E_SWIGLU}};
+    for (int kv4 = 1; kv4 <= 4; ++kv4)
+        for (auto& p : pairs) {
+            cudaError_t e = SKB_CAT(gemv_launch_m, GEMV_M)(a, kv4, p[0], p[1], 0, nullptr, false);
+            if (e != cudaSuccess) return e;
+        }
+    return cudaSuccess;
 }
 
 cudaError_t SKB_CAT(gemv_launch_m, GEMV_M)(const GemvArgs& a, int KV4, int XM, int EM, int grid,

@@ -20,5 +20,8 @@ GemvArgs gemv_args_plain(const float* x, int ldx, int N, int K);
 cudaError_t gemv_launch_m1(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
 cudaError_t gemv_launch_m2(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
 cudaError_t gemv_launch_m4(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
+cudaError_t gemv_prepare_m1();
+cudaError_t gemv_prepare_m2();
+cudaError_t gemv_prepare_m4();
 
 }  // namespace skb

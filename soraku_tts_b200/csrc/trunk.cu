@@ -47,13 +47,22 @@ __device__ __forceinline__ float4 norm_rope_head(float4 x, const float* w, float
     return x;
 }
 
-// grid (S, KVH, R), 256 threads, dynamic smem n_rep * nmax floats.
+// grid (S, KVH, R), 256 threads.  CTA (s, g, r) owns positions
+// [s*T/S, (s+1)*T/S) of row r's cache for kv head g (T = cached length + 1).
+// Warp w takes positions pb+w, pb+w+8, ... in batches of 4: the K and V rows of
+// a batch (512 B each, one float4 per lane) are loaded together, scores are
+// warp-reduced, and an online softmax keeps (max, sum, o[h][lane*4..+4]) per
+// warp.  The 8 warps merge through shared memory into the CTA's partial; the
+// last CTA of each (row, kv head) -- an atomic ticket, no waiting -- merges the
+// S partials in split order and writes the attention output.
+constexpr int ATT_B = 4;
+
 __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a) {
-    extern __shared__ float sc[];
     __shared__ __align__(16) float qs[2][128];
     __shared__ __align__(16) float ks[128];
     __shared__ __align__(16) float vs[128];
-    __shared__ float sm_m[2], sm_l[2];
+    __shared__ __align__(16) float wo[8][2][128];
+    __shared__ float wm[8][2], wl[8][2];
     __shared__ int sm_last;
 
     const int s = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
@@ -81,6 +90,10 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
         const int h = g * n_rep + (warp - 1);
         float4 q = ld_cg4(reinterpret_cast<const float4*>(row + h * 128) + lane);
         q = norm_rope_head(q, a.qn, a.eps, cosr, sinr, lane, true, true);
+        q.x *= a.scale;
+        q.y *= a.scale;
+        q.z *= a.scale;
+        q.w *= a.scale;
         reinterpret_cast<float4*>(qs[warp - 1])[lane] = q;
     } else if (warp == n_rep + 1) {
         const float4 v =
@@ -91,41 +104,71 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
 
     const int pb = (int)((long long)s * T / a.S);
     const int pe = (int)((long long)(s + 1) * T / a.S);
-    const int n = pe - pb;
     if (s == a.S - 1 && tid < 128) {
         a.kv.at(a.layer, r, p_new, 0, g)[tid] = ks[tid];
         a.kv.at(a.layer, r, p_new, 1, g)[tid] = vs[tid];
     }
-    // scores: one warp per position
-    for (int p = pb + warp; p < pe; p += 8) {
-        float4 k4;
-        if (p == p_new)
-            k4 = reinterpret_cast<const float4*>(ks)[lane];
-        else
-            k4 = ld_cg4(reinterpret_cast<const float4*>(a.kv.at(a.layer, r, p, 0, g)) + lane);
-        for (int h = 0; h < n_rep; ++h) {
-            const float4 q4 = reinterpret_cast<const float4*>(qs[h])[lane];
-            float d = q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w;
-            d = warp_sum(d);
-            if (lane == 0) sc[h * a.nmax + (p - pb)] = d * a.scale;
+    float4 q4[2];
+    q4[0] = reinterpret_cast<const float4*>(qs[0])[lane];
+    q4[1] = n_rep > 1 ? reinterpret_cast<const float4*>(qs[1])[lane] : q4[0];
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float4 o[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int p0 = pb + warp; p0 < pe; p0 += 8 * ATT_B) {
+        float4 kb[ATT_B], vb[ATT_B];
+#pragma unroll
+        for (int j = 0; j < ATT_B; ++j) {
+            const int p = p0 + 8 * j;
+            if (p < pe) {
+                if (p == p_new) {
+                    kb[j] = reinterpret_cast<const float4*>(ks)[lane];
+                    vb[j] = reinterpret_cast<const float4*>(vs)[lane];
+                } else {
+                    kb[j] = ld_cg4(reinterpret_cast<const float4*>(a.kv.at(a.layer, r, p, 0, g)) + lane);
+                    vb[j] = ld_cg4(reinterpret_cast<const float4*>(a.kv.at(a.layer, r, p, 1, g)) + lane);
+                }
+            } else {
+                kb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vb[j] = kb[j];
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (h >= n_rep) break;
+            float sc[ATT_B];
+#pragma unroll
+            for (int j = 0; j < ATT_B; ++j) {
+                float d = q4[h].x * kb[j].x + q4[h].y * kb[j].y + q4[h].z * kb[j].z + q4[h].w * kb[j].w;
+                d = warp_sum(d);
+                sc[j] = (p0 + 8 * j < pe) ? d : -INFINITY;
+            }
+            float mt = sc[0];
+#pragma unroll
+            for (int j = 1; j < ATT_B; ++j) mt = fmaxf(mt, sc[j]);
+            const float mn = fmaxf(m[h], mt);
+            const float corr = expf(m[h] - mn);
+            float lsum = l[h] * corr;
+            float4 acc = make_float4(o[h].x * corr, o[h].y * corr, o[h].z * corr, o[h].w * corr);
+#pragma unroll
+            for (int j = 0; j < ATT_B; ++j) {
+                const float e = expf(sc[j] - mn);
+                lsum += e;
+                acc.x = fmaf(e, vb[j].x, acc.x);
+                acc.y = fmaf(e, vb[j].y, acc.y);
+                acc.z = fmaf(e, vb[j].z, acc.z);
+                acc.w = fmaf(e, vb[j].w, acc.w);
+            }
+            m[h] = mn;
+            l[h] = lsum;
+            o[h] = acc;
         }
     }
-    __syncthreads();
-    if (warp < n_rep) {
-        float* sh = sc + warp * a.nmax;
-        float m = -INFINITY;
-        for (int i = lane; i < n; i += 32) m = fmaxf(m, sh[i]);
-        m = warp_max(m);
-        float l = 0.f;
-        for (int i = lane; i < n; i += 32) {
-            const float e = (n > 0) ? expf(sh[i] - m) : 0.f;
-            sh[i] = e;
-            l += e;
-        }
-        l = warp_sum(l);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (h >= n_rep) break;
+        reinterpret_cast<float4*>(wo[warp][h])[lane] = o[h];
         if (lane == 0) {
-            sm_m[warp] = m;
-            sm_l[warp] = l;
+            wm[warp][h] = m[h];
+            wl[warp][h] = l[h];
         }
     }
     __syncthreads();
@@ -133,30 +176,22 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
     float* part = a.part + ((((size_t)r * a.kv.KVH + g) * a.S + s) * n_rep) * hd2;
     if (tid < n_rep * 128) {
         const int h = tid >> 7, d = tid & 127;
-        const float* sh = sc + h * a.nmax;
-        float o = 0.f;
-        int i = 0;
-        for (; i + 4 <= n; i += 4) {
-            float v0, v1, v2, v3;
-            const int p0 = pb + i;
-            v0 = (p0 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0, 1, g) + d);
-            v1 = (p0 + 1 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0 + 1, 1, g) + d);
-            v2 = (p0 + 2 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0 + 2, 1, g) + d);
-            v3 = (p0 + 3 == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p0 + 3, 1, g) + d);
-            o = fmaf(sh[i], v0, o);
-            o = fmaf(sh[i + 1], v1, o);
-            o = fmaf(sh[i + 2], v2, o);
-            o = fmaf(sh[i + 3], v3, o);
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w][h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                const float c = expf(wm[w][h] - M);
+                L = fmaf(wl[w][h], c, L);
+                O = fmaf(wo[w][h][d], c, O);
+            }
         }
-        for (; i < n; ++i) {
-            const int p = pb + i;
-            const float v = (p == p_new) ? vs[d] : __ldcg(a.kv.at(a.layer, r, p, 1, g) + d);
-            o = fmaf(sh[i], v, o);
-        }
-        part[h * hd2 + d] = o;
+        part[h * hd2 + d] = O;
         if (d == 0) {
-            part[h * hd2 + 128] = sm_m[h];
-            part[h * hd2 + 129] = sm_l[h];
+            part[h * hd2 + 128] = M;
+            part[h * hd2 + 129] = L;
         }
     }
     __threadfence();
@@ -173,7 +208,9 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
         float L = 0.f, O = 0.f;
         for (int j = 0; j < a.S; ++j) {
             const float* pj = base + ((size_t)j * n_rep + h) * hd2;
-            const float w = expf(__ldcg(pj + 128) - M);
+            const float mj = __ldcg(pj + 128);
+            if (mj == -INFINITY) continue;
+            const float w = expf(mj - M);
             L = fmaf(__ldcg(pj + 129), w, L);
             O = fmaf(__ldcg(pj + d), w, O);
         }
@@ -183,8 +220,7 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
 }
 
 cudaError_t decode_attn_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl) {
-    const size_t smem = (size_t)a.n_rep * a.nmax * sizeof(float);
-    return launch(decode_attn_kernel, dim3(a.S, a.kv.KVH, R), dim3(256), smem, s, pdl, a);
+    return launch(decode_attn_kernel, dim3(a.S, a.kv.KVH, R), dim3(256), 0, s, pdl, a);
 }
 
 // ------------------------------------------------------------------ prefill
@@ -521,10 +557,7 @@ cudaError_t prefill_attn_launch(const float* Q, const int* row_off, const int* r
 }
 
 cudaError_t trunk_init_attrs() {
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PATTN_SMEM);
-    return e;
+    return cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PATTN_SMEM);
 }
 
 cudaError_t gather_rows_launch(const float* X, const int* src, const int* dst, int n, float* out,

@@ -84,6 +84,8 @@ def _decode(model, data, n_frames, *, temperature=0.9, top_k=50, top_p=0.95, see
         torch.cuda.synchronize()
         logits.append(eng.view(4).view(model.config.num_codebooks, 2, -1).cpu().numpy().copy())
     codes = eng.read_codes(0, 0, n_frames).clone().numpy() if n_frames else np.zeros((0, 16), np.int64)
+    err = eng.view(6, torch.int32).cpu().numpy()
+    assert (err == 0).all(), f"device error flags raised: {err}"
     eng.close()
     return codes, (np.stack(logits) if logits else None), hidden0
 
