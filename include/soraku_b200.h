@@ -110,6 +110,27 @@ int skb_cfg_sample(const float *logits, int rows_per_req, int n_req, int V,
                    const skb_sample_params *params, int bos_id, int pad_id, int eos_id,
                    int64_t *codes_out, float *uniform_out, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * One decode-attention step of a Qwen3 layer (the attention half of
+ * modeling_qwen3.py Qwen3Attention.forward :240-291 for one new token per
+ * row): q/k RMSNorm over each head, neox RoPE at pos[row], append k/v at
+ * pos[row] of the paged cache, GQA softmax(q k^T / sqrt(hd)) v over positions
+ * 0..pos[row].  The engine runs the same kernel for every layer.
+ *   qkv        device [rows, (n_heads + 2 n_kv_heads) * head_dim]  (q | k | v)
+ *   rope_cos/sin device [max_len, head_dim / 2]  cos/sin of inv_freq[i] * p
+ *   pos        device int32 [rows]  position of the new token (< max_len)
+ *   kv_pool    device [n_pages][2][n_kv_heads][page_size][head_dim]
+ *   page_table device int32 [rows, max_pages]
+ *   part       scratch [rows * n_kv_heads * splits * (n_heads/n_kv_heads) * (head_dim + 2)]
+ *   tickets    scratch int32 [rows * n_kv_heads], zero before the call (left zero)
+ *   out        device [rows, n_heads * head_dim]
+ * head_dim must be 128 and n_heads / n_kv_heads 1 or 2. */
+int skb_decode_attention(const float *qkv, int rows, int n_heads, int n_kv_heads, int head_dim,
+                         const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
+                         const float *rope_sin, int max_len, const int32_t *pos, float *kv_pool,
+                         const int32_t *page_table, int max_pages, int page_size, int n_pages,
+                         int splits, float *part, int32_t *tickets, float *out, cudaStream_t stream);
+
 /* Test hooks: the device exp used by the sampler, and raw Philox4x32-10.
  * ctr_key: device uint32 [n, 6] = (c0, c1, c2, c3, k0, k1); out: [n, 4]. */
 int skb_test_exp(const float *x, float *y, int n, cudaStream_t stream);

@@ -170,6 +170,7 @@ KVLayout kv_layout(const skb_engine* e) {
     k.KVH = e->KVH;
     k.hd = e->hd;
     k.layer_floats = e->layer_floats;
+    k.n_pages = e->R * e->max_pages;
     return k;
 }
 

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
 
     int p_new = a.pos[r];
     if (p_new < 0 || p_new >= a.max_len) {
-        if (tid == 0) atomicExch(a.err, 1);
+        if (tid == 0 && a.err != nullptr) atomicExch(a.err, 1);
         p_new = p_new < 0 ? 0 : a.max_len - 1;
     }
     const int T = p_new + 1;
@@ -565,4 +565,60 @@ cudaError_t gather_rows_launch(const float* X, const int* src, const int* dst, i
     return launch(gather_rows_kernel, dim3(n), dim3(256), 0, s, false, X, src, dst, out, D);
 }
 
+int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, const float* qn, const float* kn,
+                        float eps, const float* rc, const float* rs, int max_len, const int32_t* pos, float* kv_pool,
+                        const int32_t* page_table, int max_pages, int page_size, int n_pages, int splits,
+                        float* part, int32_t* tickets, float* out, cudaStream_t stream) {
+    if (!qkv || !qn || !kn || !rc || !rs || !pos || !kv_pool || !page_table || !part || !tickets || !out)
+        return fail(SKB_ERR_ARG, "decode_attention: null pointer");
+    if (hd != 128 || KVH < 1 || H % KVH != 0 || H / KVH > 2)
+        return fail(SKB_ERR_ARG, "decode_attention: head_dim must be 128 and heads/kv_heads 1 or 2");
+    if (rows < 1 || rows > 65535 || max_len < 1 || max_pages < 1 || n_pages < 1 || splits < 1 || splits > 65535)
+        return fail(SKB_ERR_ARG, "decode_attention: bad sizes");
+    if (page_size < 1 || (page_size & (page_size - 1)) != 0 || (long long)max_pages * page_size < max_len)
+        return fail(SKB_ERR_ARG, "decode_attention: page_size must be a power of two covering max_len");
+    DecodeAttnArgs a = {};
+    a.qkv = qkv;
+    a.ld_qkv = (H + 2 * KVH) * hd;
+    a.qn = qn;
+    a.kn = kn;
+    a.eps = eps;
+    a.rope_cos = rc;
+    a.rope_sin = rs;
+    a.pos = pos;
+    a.max_len = max_len;
+    a.kv.pool = kv_pool;
+    a.kv.page_table = page_table;
+    a.kv.max_pages = max_pages;
+    int lg = 0;
+    while ((1 << lg) < page_size) ++lg;
+    a.kv.page_log2 = lg;
+    a.kv.KVH = KVH;
+    a.kv.hd = hd;
+    a.kv.layer_floats = (long long)n_pages * 2 * KVH * page_size * hd;
+    a.layer = 0;
+    a.H = H;
+    a.n_rep = H / KVH;
+    a.S = splits;
+    a.nmax = 0;
+    a.scale = 1.0f / sqrtf((float)hd);
+    a.part = part;
+    a.counters = tickets;
+    a.out = out;
+    a.err = nullptr;
+    a.kv.n_pages = n_pages;
+    cudaError_t e = decode_attn_launch(a, rows, stream, false);
+    return e == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
+}
+
 }  // namespace skb
+
+extern "C" int skb_decode_attention(const float* qkv, int rows, int n_heads, int n_kv_heads, int head_dim,
+                                    const float* q_norm, const float* k_norm, float eps, const float* rope_cos,
+                                    const float* rope_sin, int max_len, const int32_t* pos, float* kv_pool,
+                                    const int32_t* page_table, int max_pages, int page_size, int n_pages,
+                                    int splits, float* part, int32_t* tickets, float* out, cudaStream_t stream) {
+    return skb::decode_attention_op(qkv, rows, n_heads, n_kv_heads, head_dim, q_norm, k_norm, eps, rope_cos,
+                                    rope_sin, max_len, pos, kv_pool, page_table, max_pages, page_size, n_pages,
+                                    splits, part, tickets, out, stream);
+}

@@ -17,8 +17,10 @@ struct KVLayout {
     int KVH;
     int hd;
     long long layer_floats;  // floats per layer
+    int n_pages;             // pages per layer; table entries outside [0, n_pages) read page 0
     __device__ __forceinline__ float* at(int layer, int row, int pos, int kv, int g) const {
-        const int page = page_table[row * max_pages + (pos >> page_log2)];
+        int page = page_table[row * max_pages + (pos >> page_log2)];
+        if ((unsigned)page >= (unsigned)n_pages) page = 0;
         const int slot = pos & ((1 << page_log2) - 1);
         return pool + layer * layer_floats +
                ((((long long)page * 2 + kv) * KVH + g) << page_log2) * hd + (long long)slot * hd;

@@ -203,3 +203,28 @@ def _ctypes_size() -> int:
     import ctypes
 
     return ctypes.sizeof(_lib.skb_sample_params)
+
+
+def decode_attention(qkv: torch.Tensor, *, n_heads: int, n_kv_heads: int, q_norm: torch.Tensor,
+                     k_norm: torch.Tensor, eps: float, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
+                     pos: torch.Tensor, kv_pool: torch.Tensor, page_table: torch.Tensor, page_size: int,
+                     splits: int) -> torch.Tensor:
+    """One Qwen3 decode-attention step over a paged FP32 KV cache (updated in
+    place at ``pos``); see skb_decode_attention in include/soraku_b200.h."""
+    rows = qkv.shape[0]
+    hd = 128
+    n_rep = n_heads // n_kv_heads
+    for name, t in (("qkv", qkv), ("q_norm", q_norm), ("k_norm", k_norm), ("rope_cos", rope_cos),
+                    ("rope_sin", rope_sin), ("kv_pool", kv_pool)):
+        _check(t, name, tuple(t.shape))
+    _check(pos, "pos", (rows,), torch.int32)
+    _check(page_table, "page_table", tuple(page_table.shape), torch.int32)
+    part = torch.empty(rows * n_kv_heads * splits * n_rep * (hd + 2), dtype=torch.float32, device=qkv.device)
+    tickets = torch.zeros(rows * n_kv_heads, dtype=torch.int32, device=qkv.device)
+    out = torch.empty((rows, n_heads * hd), dtype=torch.float32, device=qkv.device)
+    n_pages = kv_pool.numel() // (2 * n_kv_heads * page_size * hd)
+    _lib.call("skb_decode_attention", qkv.data_ptr(), rows, n_heads, n_kv_heads, hd, q_norm.data_ptr(),
+              k_norm.data_ptr(), float(eps), rope_cos.data_ptr(), rope_sin.data_ptr(), rope_cos.shape[0],
+              pos.data_ptr(), kv_pool.data_ptr(), page_table.data_ptr(), page_table.shape[1], page_size, n_pages,
+              splits, part.data_ptr(), tickets.data_ptr(), out.data_ptr(), _stream())
+    return out
