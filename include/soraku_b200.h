@@ -131,6 +131,31 @@ int skb_decode_attention(const float *qkv, int rows, int n_heads, int n_kv_heads
                          const int32_t *page_table, int max_pages, int page_size, int n_pages,
                          int splits, float *part, int32_t *tickets, float *out, cudaStream_t stream);
 
+/* Decode attention for callers that must not allocate device memory.  It has
+ * no counterpart in the reference.  Some hosts cannot call cudaMalloc when a
+ * frame is decoded: an audio or streaming thread cannot afford the device-wide
+ * synchronisation an allocation may cause, and an application that reserves
+ * all device memory up front through its own allocator forbids raw
+ * allocations.  Such callers pass the same inputs and outputs as to
+ * skb_decode_attention but no scratch: the split partials and tickets live in
+ * one library-owned device array of SKB_NOALLOC_SCRATCH_BYTES (2 MiB + 1 KiB),
+ * which every GPU that loads this library holds until the process exits.
+ * Limit: rows * n_kv_heads * splits * (n_heads / n_kv_heads) * (head_dim + 2)
+ * floats must fit in 2 MiB and rows * n_kv_heads tickets in 1 KiB; larger
+ * calls return SKB_ERR_ARG.  The first call on a device looks up the array's
+ * device address (a one-time set-up), so make that first call before any
+ * stream capture.  All calls share the array and it keeps the last call's
+ * contents: calls that overlap on the GPU (different streams, or different
+ * host threads on one device) race and must be serialised by the caller.
+ * No cudaMalloc, cudaFree or allocating library routine is called. */
+#define SKB_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u + 1024u)
+int skb_decode_attention_noalloc(const float *qkv, int rows, int n_heads, int n_kv_heads,
+                                 int head_dim, const float *q_norm, const float *k_norm, float eps,
+                                 const float *rope_cos, const float *rope_sin, int max_len,
+                                 const int32_t *pos, float *kv_pool, const int32_t *page_table,
+                                 int max_pages, int page_size, int n_pages, int splits, float *out,
+                                 cudaStream_t stream);
+
 /* Test hooks: the device exp used by the sampler, and raw Philox4x32-10.
  * ctr_key: device uint32 [n, 6] = (c0, c1, c2, c3, k0, k1); out: [n, 4]. */
 int skb_test_exp(const float *x, float *y, int n, cudaStream_t stream);

@@ -36,6 +36,9 @@ SIGNATURES = {
     "skb_decode_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p,
                                      c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                      c_void_p, c_void_p, c_void_p, c_void_p]),
+    "skb_decode_attention_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
+                                             c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                             c_int, c_int, c_void_p, c_void_p]),
     "skb_test_exp": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "skb_test_philox": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "skb_engine_create": (c_int, [c_void_p, c_void_p, c_void_p]),
