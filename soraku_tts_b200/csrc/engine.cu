@@ -495,6 +495,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     e->max_pages = (opts->max_len + e->o.page_size - 1) / e->o.page_size;
     e->S = opts->attn_splits > 0 ? opts->attn_splits
                                  : (2 * e->nsm / (e->R * e->KVH) > 0 ? 2 * e->nsm / (e->R * e->KVH) : 1);
+    if (e->S > 512) e->S = 512;  // the split combine stages S x 2 (max, sum) pairs in 8 KB of shared memory
     e->nmax = (opts->max_len + e->S - 1) / e->S + 1;
     const size_t n_pages = (size_t)e->R * e->max_pages;
     e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;

@@ -297,6 +297,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
     if (topp_on) {
         if (tid == 0) {
             float s1 = 0.0f;
+#pragma unroll 8
             for (int j = 0; j < n; ++j) s1 = __fadd_rn(s1, e[j]);
             scf[0] = s1;
         }
@@ -307,14 +308,14 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         for (int j = tid; j < n; j += SAMPLER_THREADS) pj[j] = __fdiv_rn(e[j], s1);
         __syncthreads();
         if (tid == 0) {
+            // the whole running sum is formed (same adds in the same order as
+            // stopping at the first crossing) so the loads can be pipelined
             int keep = n;
             float cum = 0.0f;
+#pragma unroll 8
             for (int j = 0; j < n; ++j) {
                 cum = __fadd_rn(cum, pj[j]);
-                if (cum > J.top_p) {
-                    keep = j + 1;
-                    break;
-                }
+                if (cum > J.top_p && keep == n) keep = j + 1;
             }
             sc[11] = keep;
         }
@@ -325,16 +326,15 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
     if (tid == 0) {
         const int keep = sc[11];
         float s2 = 0.0f;
+#pragma unroll 8
         for (int j = 0; j < keep; ++j) s2 = __fadd_rn(s2, e[j]);
         const float t = __fmul_rn(J.u, s2);
         int pick = -1;
         float run = 0.0f;
+#pragma unroll 8
         for (int j = 0; j < keep; ++j) {
             run = __fadd_rn(run, e[j]);
-            if (run > t) {
-                pick = j;
-                break;
-            }
+            if (run > t && pick < 0) pick = j;
         }
         if (pick < 0) {
             pick = 0;

@@ -200,21 +200,31 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
     __syncthreads();
     if (!sm_last) return;
     __threadfence();
-    if (tid < n_rep * 128) {
-        const int h = tid >> 7, d = tid & 127;
+    // Merge the S split partials in split order.  The (max, sum) pairs are
+    // staged in shared memory by parallel loads first, so the weighted sum over
+    // the splits issues its partial-output loads independently of each other.
+    {
         const float* base = a.part + ((((size_t)r * a.kv.KVH + g) * a.S) * n_rep) * hd2;
-        float M = -INFINITY;
-        for (int j = 0; j < a.S; ++j) M = fmaxf(M, __ldcg(base + ((size_t)j * n_rep + h) * hd2 + 128));
-        float L = 0.f, O = 0.f;
-        for (int j = 0; j < a.S; ++j) {
-            const float* pj = base + ((size_t)j * n_rep + h) * hd2;
-            const float mj = __ldcg(pj + 128);
-            if (mj == -INFINITY) continue;
-            const float w = expf(mj - M);
-            L = fmaf(__ldcg(pj + 129), w, L);
-            O = fmaf(__ldcg(pj + d), w, O);
+        float* sm_ml = &wo[0][0][0];  // reuse: [S][n_rep][2] (S * 4 floats <= 2048)
+        for (int i = tid; i < a.S * n_rep; i += 256) {
+            sm_ml[2 * i] = __ldcg(base + (size_t)i * hd2 + 128);
+            sm_ml[2 * i + 1] = __ldcg(base + (size_t)i * hd2 + 129);
         }
-        a.out[(size_t)r * a.H * 128 + (g * n_rep + h) * 128 + d] = O / L;
+        __syncthreads();
+        if (tid < n_rep * 128) {
+            const int h = tid >> 7, d = tid & 127;
+            float M = -INFINITY;
+            for (int j = 0; j < a.S; ++j) M = fmaxf(M, sm_ml[2 * (j * n_rep + h)]);
+            float L = 0.f, O = 0.f;
+#pragma unroll 8
+            for (int j = 0; j < a.S; ++j) {
+                const float mj = sm_ml[2 * (j * n_rep + h)];
+                const float w = (mj == -INFINITY) ? 0.f : expf(mj - M);
+                L = fmaf(sm_ml[2 * (j * n_rep + h) + 1], w, L);
+                O = fmaf(__ldcg(base + ((size_t)j * n_rep + h) * hd2 + d), w, O);
+            }
+            a.out[(size_t)r * a.H * 128 + (g * n_rep + h) * 128 + d] = O / L;
+        }
     }
     if (tid == 0) a.counters[r * a.kv.KVH + g] = 0;
 }
@@ -573,7 +583,7 @@ int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, cons
         return fail(SKB_ERR_ARG, "decode_attention: null pointer");
     if (hd != 128 || KVH < 1 || H % KVH != 0 || H / KVH > 2)
         return fail(SKB_ERR_ARG, "decode_attention: head_dim must be 128 and heads/kv_heads 1 or 2");
-    if (rows < 1 || rows > 65535 || max_len < 1 || max_pages < 1 || n_pages < 1 || splits < 1 || splits > 65535)
+    if (rows < 1 || rows > 65535 || max_len < 1 || max_pages < 1 || n_pages < 1 || splits < 1 || splits > 512)
         return fail(SKB_ERR_ARG, "decode_attention: bad sizes");
     if (page_size < 1 || (page_size & (page_size - 1)) != 0 || (long long)max_pages * page_size < max_len)
         return fail(SKB_ERR_ARG, "decode_attention: page_size must be a power of two covering max_len");
