@@ -66,6 +66,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true")
+    ap.add_argument("--persistent", action="store_true", help="run frames as the persistent frame kernel")
     return ap.parse_args()
 
 
@@ -221,7 +222,8 @@ def b200_main(args, wl):
     model = SorakuModel.random(dims, 42, f"cuda:{local}")
     weights_bytes = sum(t.numel() * 4 for k, t in model.params.items() if k != "trunk.embed_tokens.weight")
     gen = FastGenerator(model, device=torch.device("cuda", local), frames_per_graph=fpg,
-                        use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch)
+                        use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch,
+                        persistent=args.persistent)
     ids, uncond, prompt = make_inputs(1000 + rank, wl["n_text"], wl["n_ref"])
     gkw = dict(max_new_frames=frames, min_new_frames=frames, **SAMPLING)
 
@@ -345,6 +347,7 @@ def b200_main(args, wl):
             "global_batch": world, "rows_per_gpu": 2, "seq_len": 2 + wl["n_text"] + wl["n_ref"] + frames,
             "parallelism": "replicas" if world > 1 else "single",
             "frames_per_graph": fpg, "pdl": not args.no_pdl, "l2_prefetch": not args.no_prefetch,
+            "persistent_kernel": eng.is_persistent(),
             "rtf": round(FRAME_RATE / (value / world), 5), "prefill_ms": round(statistics.mean(pre_ms), 2),
             "frame_ms": round(frame_ms, 4), "l2": "inputs larger than L2: each frame streams ~2.1 GB",
             "wall_s_value_region": round(t_wall, 3),
@@ -356,7 +359,7 @@ def b200_main(args, wl):
                      "peak_kind": peak_kind, "launch_ms": round(k_ms, 5), "bytes_per_launch": k_bytes},
         "roofline_frame": {"bound": "hbm", "achieved": round(f_gbs, 1), "peak": peak, "unit": "GB/s",
                            "frac": round(f_gbs / peak, 4), "bytes_per_frame": int(bpf), "peak_kind": peak_kind},
-        "gpu_launches": int(eng.kernels_per_frame() * frames * args.steps),
+        "gpu_launches": int(eng.launches_per_step() * (frames // fpg) * args.steps),
         "clocks": clk,
     }
     if cpu is not None:

@@ -125,6 +125,27 @@ __device__ __forceinline__ float butterfly_reduce(float (&v)[N], int lane) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// Barrier policies for code shared by standalone kernels (every thread of the
+// CTA takes part) and the persistent frame kernel (only its 256 consumer
+// threads take part; the producer warp runs independently).
+struct BlockSync {
+    __device__ __forceinline__ static void sync() { __syncthreads(); }
+};
+struct ConsumerSync {
+    __device__ __forceinline__ static void sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+    // Barrier that also returns the AND of `p` over the 256 consumer threads,
+    // so a decision taken per thread becomes uniform.
+    __device__ __forceinline__ static bool sync_and(bool p) {
+        int r;
+        asm volatile(
+            "{\n .reg .pred a, b;\n setp.ne.s32 a, %1, 0;\n bar.red.and.pred b, 1, 256, a;\n selp.s32 %0, 1, 0, b;\n}\n"
+            : "=r"(r)
+            : "r"((int)p)
+            : "memory");
+        return r != 0;
+    }
+};
+
 // ------------------------------------------------------ bulk copy + mbarrier
 // 1-D bulk copies (TMA engine, no tensor map) from global memory into this
 // CTA's shared memory, completing on an mbarrier.  No multicast: the source is

@@ -26,36 +26,13 @@
 #include <functional>
 #include <vector>
 
+#include "engine_types.cuh"
+#include "frame.cuh"
 #include "ops.cuh"
 #include "sampler.cuh"
 #include "trunk_api.cuh"
 
 namespace skb {
-
-struct ReqState {
-    float cfg, temp, temp_q0, top_p, top_p_q0;
-    int top_k, top_k_q0, min_new_frames, eos_rule;
-    int frame;  // frames completed (advanced by the q = Q-1 sampler)
-    int done;   // q0 drew EOS at least once
-    int pad_;
-    unsigned long long seed;
-};
-
-struct DepthSampleArgs {
-    const float* logits;  // [R][V]
-    int rows_per_req, V, q, Q, D;
-    ReqState* st;
-    const int* host_flag;
-    const float* table;
-    float scale;
-    float* prefix;  // [n_req][D]
-    float* x;       // [R][D]
-    int64_t* cur_codes;  // [n_req][Q]
-    int64_t* hist;       // [n_req][max_frames][Q]
-    int max_frames;
-    int bos, pad, eos;
-    PrefetchList pf;
-};
 
 __global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const DepthSampleArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -63,50 +40,7 @@ __global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const Dep
     prefetch_share(a.pf, blockIdx.x, gridDim.x);
     pdl_wait();
     pdl_trigger();
-    const int r = blockIdx.x, tid = threadIdx.x;
-    ReqState* st = a.st + r;
-    const int frame = __ldcg(&st->frame);
-    const bool q0 = a.q == 0;
-    SampleJob J;
-    J.cond = a.logits + (size_t)r * a.rows_per_req * a.V;
-    J.uncond = a.rows_per_req > 1 ? J.cond + a.V : nullptr;
-    J.V = a.V;
-    J.cfg_scale = st->cfg;
-    J.temperature = q0 ? st->temp_q0 : st->temp;
-    J.top_k = q0 ? st->top_k_q0 : st->top_k;
-    J.top_p = q0 ? st->top_p_q0 : st->top_p;
-    J.mask_eos = !q0 ? 1 : (st->eos_rule == 0 ? (__ldcg(a.host_flag) != 0) : (frame < st->min_new_frames));
-    J.bos = a.bos;
-    J.pad = a.pad;
-    J.eos = a.eos;
-    J.u = philox_uniform(st->seed, (uint32_t)r, (uint32_t)frame, (uint32_t)a.q);
-    const int code = sample_one(J, smem);
-    if (tid == 0) {
-        a.cur_codes[(size_t)r * a.Q + a.q] = code;
-        if (frame < a.max_frames) a.hist[((size_t)r * a.max_frames + frame) * a.Q + a.q] = code;
-        if (q0 && code == a.eos) st->done = 1;
-    }
-    float* pr = a.prefix + (size_t)r * a.D;
-    if (a.q < a.Q - 1) {
-        const float* trow = a.table + ((size_t)a.q * a.V + code) * a.D;
-        for (int i = tid; i < a.D; i += SAMPLER_THREADS) pr[i] = __ldcg(pr + i) + trow[i] * a.scale;
-    } else {
-        if (tid < a.Q) codes_s[tid] = (tid == a.q) ? code : (int)__ldcg(a.cur_codes + (size_t)r * a.Q + tid);
-        __syncthreads();
-        for (int i = tid; i < a.D; i += SAMPLER_THREADS) {
-            float acc = 0.f;
-            for (int qq = 0; qq < a.Q; ++qq) {
-                int c = codes_s[qq];
-                if (c < 0 || c >= a.V) c = 0;
-                const float v = a.table[((size_t)qq * a.V + c) * a.D + i];
-                acc = (qq == 0) ? v : acc + v;
-            }
-            acc = acc * a.scale;
-            for (int rr = 0; rr < a.rows_per_req; ++rr) a.x[((size_t)r * a.rows_per_req + rr) * a.D + i] = acc;
-            pr[i] = 0.f;
-        }
-        if (tid == 0) st->frame = frame + 1;
-    }
+    depth_sample_body<BlockSync, SAMPLER_VMAX>(a, blockIdx.x, smem, codes_s);
 }
 
 }  // namespace skb
@@ -143,6 +77,16 @@ struct skb_engine {
     std::vector<int> frames_host, pos_host;
     std::vector<ReqState> st_host;
     std::vector<void*> allocs;
+    // persistent frame kernel
+    Phase* d_prog = nullptr;
+    int max_prog = 0;
+    unsigned* bar_count = nullptr;
+    int graph_persistent = 0;  // the captured step runs the persistent kernel
+    int persistent_direct = 0; // ... launched directly (the graph capture was refused)
+    FrameArgs fargs = {};
+    int fk_M = 0;
+    unsigned long long* timeline = nullptr;  // persistent-kernel phase timestamps (debug)
+    unsigned long long* cta_end = nullptr;   // per-CTA phase end stamps (debug, up to 8 frames)
 };
 
 namespace {
@@ -221,8 +165,21 @@ Node gemv_node(const skb_engine* e, GemvArgs a, int M, int XM, int EM) {
     return n;
 }
 
-std::vector<Node> build_frame(skb_engine* e, int n_active) {
-    std::vector<Node> nodes;
+Phase gemv_phase(const GemvArgs& a, int XM, int EM) {
+    Phase ph = {};
+    ph.kind = PH_GEMV;
+    ph.xm = XM;
+    ph.em = EM;
+    ph.kv4 = ((a.K >> 2) + GEMV_THREADS - 1) / GEMV_THREADS;
+    ph.g = a;
+    return ph;
+}
+
+// The frame as a program of phases (16 depth steps, then the trunk layers).
+// Both execution paths are built from it: separate kernels chained with PDL
+// (build_frame) or the persistent frame kernel (the program uploaded as is).
+std::vector<Phase> build_phases(skb_engine* e, int n_active) {
+    std::vector<Phase> phases;
     const int R = n_active * e->rpr;
     const int D = e->D;
     for (int q = 0; q < e->Q; ++q) {
@@ -243,7 +200,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.hout = e->hidden;
             a.out = e->act;
             a.ldo = e->I;
-            nodes.push_back(gemv_node(e, a, R, X_NORM_ADD_NORM, E_SWIGLU));
+            phases.push_back(gemv_phase(a, X_NORM_ADD_NORM, E_SWIGLU));
         }
         {  // D_down
             GemvArgs a = gemv_args_plain(e->act, e->I, D, e->I);
@@ -252,7 +209,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.ldr = D;
             a.out = e->y;
             a.ldo = D;
-            nodes.push_back(gemv_node(e, a, R, X_PLAIN, E_RESID));
+            phases.push_back(gemv_phase(a, X_PLAIN, E_RESID));
         }
         {  // D_cls
             GemvArgs a = gemv_args_plain(e->y, D, e->V, D);
@@ -262,9 +219,9 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.bias = e->m.depth_bias + (size_t)q * e->V;
             a.out = lg;
             a.ldo = e->V;
-            nodes.push_back(gemv_node(e, a, R, X_RMSNORM, E_BIAS));
+            phases.push_back(gemv_phase(a, X_RMSNORM, E_BIAS));
         }
-        {  // D_samp
+        {  // D_samp: the classifier phase's sampler
             DepthSampleArgs a = {};
             a.logits = lg;
             a.rows_per_req = e->rpr;
@@ -284,14 +241,10 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.bos = e->m.bos_id;
             a.pad = e->m.pad_id;
             a.eos = e->m.eos_id;
-            Node n;
-            n.ctas = n_active;
-            n.run = [a, n_active](cudaStream_t s, bool pdl, const PrefetchList& pf) {
-                DepthSampleArgs b = a;
-                b.pf = pf;
-                return launch(depth_sample_kernel, dim3(n_active), dim3(SAMPLER_THREADS), SAMPLER_SMEM, s, pdl, b);
-            };
-            nodes.push_back(n);
+            Phase& cls = phases.back();
+            cls.sample = 1;
+            cls.n_req = n_active;
+            cls.s = a;
         }
     }
     const int qd = e->H * e->hd, kvd = e->KVH * e->hd;
@@ -307,7 +260,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.neps = e->m.rms_eps;
             a.out = e->qkv;
             a.ldo = qd + 2 * kvd;
-            nodes.push_back(gemv_node(e, a, R, X_RMSNORM, E_STORE));
+            phases.push_back(gemv_phase(a, X_RMSNORM, E_STORE));
         }
         {  // ATTN
             DecodeAttnArgs a = {};
@@ -331,14 +284,11 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.counters = e->counters;
             a.out = e->attn;
             a.err = e->err;
-            Node n;
-            n.ctas = a.S * e->KVH * R;
-            n.run = [a, R](cudaStream_t s, bool pdl, const PrefetchList& pf) {
-                DecodeAttnArgs b = a;
-                b.pf = pf;
-                return decode_attn_launch(b, R, s, pdl);
-            };
-            nodes.push_back(n);
+            Phase ph = {};
+            ph.kind = PH_ATTN;
+            ph.attn_rows = R;
+            ph.at = a;
+            phases.push_back(ph);
         }
         {  // O
             GemvArgs a = gemv_args_plain(e->attn, qd, D, qd);
@@ -347,7 +297,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.ldr = D;
             a.out = e->x;
             a.ldo = D;
-            nodes.push_back(gemv_node(e, a, R, X_PLAIN, E_RESID));
+            phases.push_back(gemv_phase(a, X_PLAIN, E_RESID));
         }
         {  // GU
             GemvArgs a = gemv_args_plain(e->x, D, 2 * e->F, D);
@@ -358,7 +308,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             a.neps = e->m.rms_eps;
             a.out = e->act;
             a.ldo = e->F;
-            nodes.push_back(gemv_node(e, a, R, X_RMSNORM, E_SWIGLU));
+            phases.push_back(gemv_phase(a, X_RMSNORM, E_SWIGLU));
         }
         {  // DOWN
             GemvArgs a = gemv_args_plain(e->act, e->F, D, e->F);
@@ -371,7 +321,41 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
                 a.inc = e->pos;
                 a.n_inc = R;
             }
-            nodes.push_back(gemv_node(e, a, R, X_PLAIN, E_RESID));
+            phases.push_back(gemv_phase(a, X_PLAIN, E_RESID));
+        }
+    }
+    return phases;
+}
+
+// Separate kernels: one GEMV launch per GEMV phase (+ the sampler after the
+// classifier), one attention launch per attention phase.
+std::vector<Node> build_frame(skb_engine* e, int n_active) {
+    const int R = n_active * e->rpr;
+    std::vector<Node> nodes;
+    for (const Phase& ph : build_phases(e, n_active)) {
+        if (ph.kind == PH_GEMV) {
+            nodes.push_back(gemv_node(e, ph.g, R, ph.xm, ph.em));
+            if (ph.sample) {
+                const DepthSampleArgs a = ph.s;
+                Node n;
+                n.ctas = n_active;
+                n.run = [a, n_active](cudaStream_t s, bool pdl, const PrefetchList& pf) {
+                    DepthSampleArgs b = a;
+                    b.pf = pf;
+                    return launch(depth_sample_kernel, dim3(n_active), dim3(SAMPLER_THREADS), SAMPLER_SMEM, s, pdl, b);
+                };
+                nodes.push_back(n);
+            }
+        } else {
+            const DecodeAttnArgs a = ph.at;
+            Node n;
+            n.ctas = a.S * e->KVH * R;
+            n.run = [a, R](cudaStream_t s, bool pdl, const PrefetchList& pf) {
+                DecodeAttnArgs b = a;
+                b.pf = pf;
+                return decode_attn_launch(b, R, s, pdl);
+            };
+            nodes.push_back(n);
         }
     }
     return nodes;
@@ -422,6 +406,30 @@ void destroy_graph(skb_engine* e) {
     e->exec = nullptr;
     e->graph_active = 0;
     e->graph_fpg = 0;
+    e->graph_persistent = 0;
+    e->persistent_direct = 0;
+}
+
+// The persistent kernel serves a model when every GEMV phase's inner size is
+// 1024, 2048 or 3072 (the ring-slot chunking it is compiled for), the CFG rows
+// are 1, 2 or 4, the audio vocabulary fits its sampler, and one CTA fits per SM.
+bool persistent_fits(const skb_engine* e, const std::vector<Phase>& phases, int R) {
+    if (R != 1 && R != 2 && R != 4) return false;
+    if (e->V > FK_VMAX) return false;
+    if ((int)phases.size() > e->max_prog) return false;
+    for (const Phase& ph : phases)
+        if (ph.kind == PH_GEMV && (ph.g.K % 1024 != 0 || ph.g.K > 3072)) return false;
+    if (frame_kernel_prepare(R) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return frame_kernel_occupancy(R) >= 1;
+}
+
+int launch_persistent(skb_engine* e, cudaStream_t s) {
+    cudaError_t err = cudaMemsetAsync(e->bar_count, 0, sizeof(unsigned), s);
+    if (err == cudaSuccess) err = frame_kernel_launch(e->fk_M, e->fargs, e->nsm, s);
+    return err == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "persistent frame kernel: %s", cudaGetErrorString(err));
 }
 
 int upload_state(skb_engine* e, int req, cudaStream_t s) {
@@ -493,8 +501,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     while ((1 << e->page_log2) < ps) ++e->page_log2;
     e->o.page_size = 1 << e->page_log2;
     e->max_pages = (opts->max_len + e->o.page_size - 1) / e->o.page_size;
-    e->S = opts->attn_splits > 0 ? opts->attn_splits
-                                 : (2 * e->nsm / (e->R * e->KVH) > 0 ? 2 * e->nsm / (e->R * e->KVH) : 1);
+    // one (row, kv head, split) item per SM
+    e->S = opts->attn_splits > 0 ? opts->attn_splits : (e->nsm / (e->R * e->KVH) > 0 ? e->nsm / (e->R * e->KVH) : 1);
     if (e->S > 512) e->S = 512;  // the split combine stages S x 2 (max, sum) pairs in 8 KB of shared memory
     e->nmax = (opts->max_len + e->S - 1) / e->S + 1;
     const size_t n_pages = (size_t)e->R * e->max_pages;
@@ -522,7 +530,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->pos, e->R)
     A(e->counters, (size_t)e->R * e->KVH)
     A(e->page_table, (size_t)e->R * e->max_pages)
-    A(e->err, 4)
+    A(e->err, 8)
+    A(e->bar_count, 1)
     A(e->host_flag, 1)
     A(e->cur_codes, (size_t)e->nreq * e->Q)
     A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
@@ -538,6 +547,10 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->ptok, T)
     A(e->pframes, (size_t)(opts->max_prefill + 1) * e->Q)
     A(e->pmeta, 5 * 8)
+    e->max_prog = e->Q * 3 + e->L * 5;
+    A(e->d_prog, e->max_prog)
+    A(e->timeline, (size_t)64 * e->max_prog * 2)
+    A(e->cta_end, (size_t)8 * e->max_prog * e->nsm)
 #undef A
     if (st != SKB_OK) {
         skb_engine_destroy(e);
@@ -786,10 +799,46 @@ int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream
     if (n_active < 1 || n_active > e->nreq || fpg < 1 || fpg > 64)
         return fail(SKB_ERR_ARG, "capture: n_active %d (1..%d), frames_per_graph %d (1..64)", n_active, e->nreq, fpg);
     destroy_graph(e);
-    const std::vector<Node> nodes = build_frame(e, n_active);
     cudaStream_t cs = e->cap_stream;
     cudaError_t err = cudaStreamSynchronize(stream);
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "capture sync: %s", cudaGetErrorString(err));
+    if (e->o.persistent) {
+        const std::vector<Phase> phases = build_phases(e, n_active);
+        const int R = n_active * e->rpr;
+        if (persistent_fits(e, phases, R)) {
+            err = cudaMemcpy(e->d_prog, phases.data(), sizeof(Phase) * phases.size(), cudaMemcpyHostToDevice);
+            if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "program upload: %s", cudaGetErrorString(err));
+            e->fk_M = R;
+            e->fargs.prog = e->d_prog;
+            e->fargs.n_phases = (int)phases.size();
+            e->fargs.frames = fpg;
+            e->fargs.bar_count = e->bar_count;
+            e->fargs.abort_flag = e->err + 4;
+            e->fargs.err = e->err;
+            e->fargs.sample_ticket = e->err + 5;
+            e->fargs.timeline = e->debug ? e->timeline : nullptr;
+            e->fargs.cta_end = (e->debug && fpg <= 8) ? e->cta_end : nullptr;
+            e->graph_active = n_active;
+            e->graph_fpg = fpg;
+            e->graph_persistent = 1;
+            cudaGraph_t graph = nullptr;
+            err = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+            int st = err == cudaSuccess ? launch_persistent(e, cs) : SKB_ERR_CUDA;
+            cudaError_t end = err == cudaSuccess ? cudaStreamEndCapture(cs, &graph) : err;
+            if (st == SKB_OK && end == cudaSuccess && graph &&
+                cudaGraphInstantiate(&e->exec, graph, 0) == cudaSuccess) {
+                cudaGraphDestroy(graph);
+                return SKB_OK;
+            }
+            // the cooperative launch could not be recorded: launch it directly per step
+            cudaGetLastError();
+            if (graph) cudaGraphDestroy(graph);
+            e->exec = nullptr;
+            e->persistent_direct = 1;
+            return SKB_OK;
+        }
+    }
+    const std::vector<Node> nodes = build_frame(e, n_active);
     for (int attempt = 0; attempt < 2; ++attempt) {
         const bool pdl = e->o.use_pdl && attempt == 0;
         cudaGraph_t graph = nullptr;
@@ -841,13 +890,20 @@ static void advance_host(skb_engine* e, int n_active, int frames) {
 
 int skb_engine_step(skb_engine* e, int mask_eos_q0, cudaStream_t stream) {
     if (!e) return fail(SKB_ERR_ARG, "step: null engine");
-    if (!e->exec) return fail(SKB_ERR_STATE, "call capture() first");
+    if (!e->exec && !e->persistent_direct) return fail(SKB_ERR_STATE, "call capture() first");
     int st = check_capacity(e, e->graph_active, e->graph_fpg);
     if (st) return st;
     static thread_local int flag_val;
     flag_val = mask_eos_q0 ? 1 : 0;
     cudaError_t err = cudaMemcpyAsync(e->host_flag, &flag_val, sizeof(int), cudaMemcpyHostToDevice, stream);
-    if (err == cudaSuccess) err = cudaGraphLaunch(e->exec, stream);
+    if (err == cudaSuccess) {
+        if (e->persistent_direct) {
+            st = launch_persistent(e, stream);
+            if (st) return st;
+        } else {
+            err = cudaGraphLaunch(e->exec, stream);
+        }
+    }
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "step: %s", cudaGetErrorString(err));
     advance_host(e, e->graph_active, e->graph_fpg);
     return SKB_OK;
@@ -891,8 +947,10 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 3: *ptr = e->pos; *numel = e->R; break;
         case 4: *ptr = e->logits_hist; *numel = (int64_t)e->Q * e->R * e->V; break;
         case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
-        case 6: *ptr = e->err; *numel = 4; break;
+        case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
+        case 8: *ptr = e->timeline; *numel = (int64_t)64 * e->max_prog * 2; break;
+        case 9: *ptr = e->cta_end; *numel = (int64_t)8 * e->max_prog * e->nsm; break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }
     return SKB_OK;
@@ -909,5 +967,13 @@ int skb_engine_kernels_per_frame(skb_engine* e) {
     if (!e) return -1;
     return e->Q * 4 + e->L * 5;
 }
+
+int skb_engine_launches_per_step(skb_engine* e) {
+    if (!e) return -1;
+    if (!e->exec && !e->persistent_direct) return 0;
+    return e->graph_persistent ? 1 : e->graph_fpg * skb_engine_kernels_per_frame(e);
+}
+
+int skb_engine_is_persistent(skb_engine* e) { return e ? e->graph_persistent : -1; }
 
 }  // extern "C"

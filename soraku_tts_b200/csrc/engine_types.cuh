@@ -1,0 +1,90 @@
+// Engine state shared by the multi-kernel frame and the persistent frame
+// kernel: per-request sampling state and the depth-sampler step.
+#pragma once
+
+#include "common.cuh"
+#include "sampler.cuh"
+
+namespace skb {
+
+struct ReqState {
+    float cfg, temp, temp_q0, top_p, top_p_q0;
+    int top_k, top_k_q0, min_new_frames, eos_rule;
+    int frame;  // frames completed (advanced by the q = Q-1 sampler)
+    int done;   // q0 drew EOS at least once
+    int pad_;
+    unsigned long long seed;
+};
+
+struct DepthSampleArgs {
+    const float* logits;  // [R][V]
+    int rows_per_req, V, q, Q, D;
+    ReqState* st;
+    const int* host_flag;
+    const float* table;
+    float scale;
+    float* prefix;  // [n_req][D]
+    float* x;       // [R][D]
+    int64_t* cur_codes;  // [n_req][Q]
+    int64_t* hist;       // [n_req][max_frames][Q]
+    int max_frames;
+    int bos, pad, eos;
+    PrefetchList pf;
+};
+
+// One request's sampling step for codebook a.q and its epilogue: the code goes
+// to the current-frame and history buffers, the prefix grows by
+// table[q][code] * scale, and after the last codebook the frame embedding
+// (sum over q in order, then * scale) becomes both CFG rows' residual stream,
+// the prefix is cleared and the request's frame counter advances.
+// Threads 0..255 take part.  codes_s: 32 ints of shared memory.
+template <class Sync, int VMAX>
+__device__ void depth_sample_body(const DepthSampleArgs& a, int r, unsigned char* smem, int* codes_s) {
+    const int tid = threadIdx.x;
+    ReqState* st = a.st + r;
+    const int frame = __ldcg(&st->frame);
+    const bool q0 = a.q == 0;
+    SampleJob J;
+    J.cond = a.logits + (size_t)r * a.rows_per_req * a.V;
+    J.uncond = a.rows_per_req > 1 ? J.cond + a.V : nullptr;
+    J.V = a.V;
+    J.cfg_scale = st->cfg;
+    J.temperature = q0 ? st->temp_q0 : st->temp;
+    J.top_k = q0 ? st->top_k_q0 : st->top_k;
+    J.top_p = q0 ? st->top_p_q0 : st->top_p;
+    J.mask_eos = !q0 ? 1 : (st->eos_rule == 0 ? (__ldcg(a.host_flag) != 0) : (frame < st->min_new_frames));
+    J.bos = a.bos;
+    J.pad = a.pad;
+    J.eos = a.eos;
+    J.u = philox_uniform(st->seed, (uint32_t)r, (uint32_t)frame, (uint32_t)a.q);
+    const int code = sample_one<Sync, VMAX>(J, smem);
+    if (tid == 0) {
+        a.cur_codes[(size_t)r * a.Q + a.q] = code;
+        if (frame < a.max_frames) a.hist[((size_t)r * a.max_frames + frame) * a.Q + a.q] = code;
+        if (q0 && code == a.eos) st->done = 1;
+    }
+    float* pr = a.prefix + (size_t)r * a.D;
+    if (a.q < a.Q - 1) {
+        const float* trow = a.table + ((size_t)a.q * a.V + code) * a.D;
+        for (int i = tid; i < a.D; i += SAMPLER_THREADS) pr[i] = __ldcg(pr + i) + trow[i] * a.scale;
+    } else {
+        if (tid < a.Q) codes_s[tid] = (tid == a.q) ? code : (int)__ldcg(a.cur_codes + (size_t)r * a.Q + tid);
+        Sync::sync();
+        for (int i = tid; i < a.D; i += SAMPLER_THREADS) {
+            float acc = 0.f;
+            for (int qq = 0; qq < a.Q; ++qq) {
+                int c = codes_s[qq];
+                if (c < 0 || c >= a.V) c = 0;
+                const float v = a.table[((size_t)qq * a.V + c) * a.D + i];
+                acc = (qq == 0) ? v : acc + v;
+            }
+            acc = acc * a.scale;
+            for (int rr = 0; rr < a.rows_per_req; ++rr) a.x[((size_t)r * a.rows_per_req + rr) * a.D + i] = acc;
+            pr[i] = 0.f;
+        }
+        if (tid == 0) st->frame = frame + 1;
+    }
+}
+
+
+}  // namespace skb

@@ -86,17 +86,17 @@ struct GemvShape {
 };
 
 // Block-wide sum of M values (one per row); every thread gets the results.
-template <int M>
+template <int M, class Sync = BlockSync>
 __device__ __forceinline__ void block_sum_rows(float (&v)[M], float* red /* [GEMV_WARPS * M] */) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int m = 0; m < M; ++m) v[m] = warp_sum(v[m]);
-    __syncthreads();
+    Sync::sync();
     if (lane == 0) {
 #pragma unroll
         for (int m = 0; m < M; ++m) red[warp * M + m] = v[m];
     }
-    __syncthreads();
+    Sync::sync();
 #pragma unroll
     for (int m = 0; m < M; ++m) {
         float s = 0.f;
@@ -108,7 +108,7 @@ __device__ __forceinline__ void block_sum_rows(float (&v)[M], float* red /* [GEM
 
 // Loads this thread's K-slice of the M activation rows, applying the norm
 // prologue.  Columns beyond K read as zero.
-template <int M, int KV4, int XM>
+template <int M, int KV4, int XM, class Sync = BlockSync>
 __device__ __forceinline__ void gemv_load_x(const GemvArgs& a, float4 (&xv)[M][KV4], float* red) {
     const int tid = threadIdx.x;
     const int K4 = a.K >> 2;
@@ -135,7 +135,7 @@ __device__ __forceinline__ void gemv_load_x(const GemvArgs& a, float4 (&xv)[M][K
                      xv[m][j].w * xv[m][j].w;
             ss[m] = s;
         }
-        block_sum_rows<M>(ss, red);
+        block_sum_rows<M, Sync>(ss, red);
 #pragma unroll
         for (int m = 0; m < M; ++m) {
             const float inv = rsqrtf(ss[m] / (float)a.K + a.neps2);
@@ -183,7 +183,7 @@ __device__ __forceinline__ void gemv_load_x(const GemvArgs& a, float4 (&xv)[M][K
                  xv[m][j].w * xv[m][j].w;
         ss[m] = s;
     }
-    block_sum_rows<M>(ss, red);
+    block_sum_rows<M, Sync>(ss, red);
 #pragma unroll
     for (int m = 0; m < M; ++m) {
         const float inv = rsqrtf(ss[m] / (float)a.K + a.neps);
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
 
     pdl_wait();
     pdl_trigger();
-    if (a.inc != nullptr && blockIdx.x == 0 && tid < a.n_inc) a.inc[tid] += 1;
+    if (a.inc != nullptr && blockIdx.x == 0 && tid < a.n_inc) atomicAdd(a.inc + tid, 1);
 
     float4 xv[M][KV4];
     gemv_load_x<M, KV4, XM>(a, xv, nred);
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
                     float sum = 0.f;
 #pragma unroll
                     for (int w = 0; w < GEMV_WARPS; ++w) sum += red[buf][w][rc * M + m];
-                    if (EM == E_RESID) sum += a.resid[(size_t)m * a.ldr + r];
+                    if (EM == E_RESID) sum += __ldcg(a.resid + (size_t)m * a.ldr + r);
                     if (EM == E_BIAS) sum += __ldg(a.bias + r);
                     a.out[(size_t)m * a.ldo + r] = sum;
                 }

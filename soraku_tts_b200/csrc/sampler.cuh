@@ -121,6 +121,7 @@ struct SampleJob {
 };
 
 // Block-wide exclusive scan of one int per thread (256 threads).
+template <class Sync>
 __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp /* [8] */, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int x = v;
@@ -130,7 +131,7 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp /* [8] */, i
         if (lane >= o) x += y;
     }
     if (lane == 31) tmp[warp] = x;
-    __syncthreads();
+    Sync::sync();
     int wprefix = 0, tot = 0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
@@ -138,20 +139,28 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp /* [8] */, i
         if (w < warp) wprefix += t;
         tot += t;
     }
-    __syncthreads();
+    Sync::sync();
     *total = tot;
     return wprefix + x - v;
 }
 
-// Returns the drawn code (same value in every thread).  smem: SAMPLER_SMEM
-// bytes of dynamic shared memory, 16-byte aligned.  Requires V <= SAMPLER_VMAX.
+// Shared memory a sampler with vocabulary capacity VMAX needs.
+template <int VMAX>
+constexpr size_t sampler_smem_bytes() {
+    return (size_t)VMAX * 16 + SAMPLER_BINS * 4 + 256;
+}
+
+// Returns the drawn code (same value in every thread).  smem:
+// sampler_smem_bytes<VMAX>() bytes of shared memory, 16-byte aligned.
+// Requires V <= VMAX and exactly 256 participating threads (0..255).
+template <class Sync = BlockSync, int VMAX = SAMPLER_VMAX>
 static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n_kept_out = nullptr) {
-    float* f = reinterpret_cast<float*>(smem);
+    constexpr int NPT = (VMAX + SAMPLER_THREADS - 1) / SAMPLER_THREADS;  // logits per thread
     unsigned long long* sorted = reinterpret_cast<unsigned long long*>(smem);
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem + (size_t)SAMPLER_VMAX * 8);
-    float* e = reinterpret_cast<float*>(smem + (size_t)SAMPLER_VMAX * 8);
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + (size_t)SAMPLER_VMAX * 16);
-    int* sc = reinterpret_cast<int*>(smem + (size_t)SAMPLER_VMAX * 16 + SAMPLER_BINS * 4);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem + (size_t)VMAX * 8);
+    float* e = reinterpret_cast<float*>(smem + (size_t)VMAX * 8);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + (size_t)VMAX * 16);
+    int* sc = reinterpret_cast<int*>(smem + (size_t)VMAX * 16 + SAMPLER_BINS * 4);
     // sc[0..7] scan tmp, sc[8] count, sc[9] bin, sc[10] n_keep_topk, sc[11] keep, sc[12] pick,
     // sc[16..] reduction scratch
     float* scf = reinterpret_cast<float*>(sc + 16);
@@ -160,29 +169,34 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
     const int V = J.V;
     const bool greedy = !(J.temperature > 0.0f);
 
-    for (int i = tid; i < V; i += SAMPLER_THREADS) {
-        float c = __ldcg(J.cond + i);
-        float m;
-        if (J.uncond != nullptr) {
-            const float un = __ldcg(J.uncond + i);
-            m = __fadd_rn(un, __fmul_rn(J.cfg_scale, __fsub_rn(c, un)));
-        } else {
-            m = c;
-        }
-        if (i == J.bos || i == J.pad || (J.mask_eos && i == J.eos)) m = -INFINITY;
-        if (!greedy) m = __fadd_rn(__fdiv_rn(m, J.temperature), 0.0f);
-        f[i] = m;
+    // All of this thread's logits are requested before any is used (one L2
+    // round trip, not one per element); f stays in registers.
+    float cv[NPT], uv[NPT], fv[NPT];
+#pragma unroll
+    for (int k = 0; k < NPT; ++k) {
+        const int i = tid + k * SAMPLER_THREADS;
+        cv[k] = i < V ? __ldcg(J.cond + i) : 0.f;
+        uv[k] = (i < V && J.uncond != nullptr) ? __ldcg(J.uncond + i) : 0.f;
     }
-    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NPT; ++k) {
+        const int i = tid + k * SAMPLER_THREADS;
+        float m = cv[k];
+        if (J.uncond != nullptr) m = __fadd_rn(uv[k], __fmul_rn(J.cfg_scale, __fsub_rn(cv[k], uv[k])));
+        if (i == J.bos || i == J.pad || (J.mask_eos && i == J.eos) || i >= V) m = -INFINITY;
+        if (!greedy) m = __fadd_rn(__fdiv_rn(m, J.temperature), 0.0f);
+        fv[k] = m;
+    }
 
     if (greedy) {
         // first maximal index
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int i = tid; i < V; i += SAMPLER_THREADS) {
-            const float v = f[i];
-            if (v > bv || (v == bv && i < bi)) {
-                bv = v;
+#pragma unroll
+        for (int k = 0; k < NPT; ++k) {
+            const int i = tid + k * SAMPLER_THREADS;
+            if (i < V && (fv[k] > bv || (fv[k] == bv && i < bi))) {
+                bv = fv[k];
                 bi = i;
             }
         }
@@ -199,7 +213,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
             scf[tid >> 5] = bv;
             sc[8 + (tid >> 5) + 16] = bi;
         }
-        __syncthreads();
+        Sync::sync();
         if (tid == 0) {
             float b = scf[0];
             int idx = sc[8 + 16];
@@ -214,10 +228,10 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
             sc[12] = idx;
             sc[11] = 1;
         }
-        __syncthreads();
+        Sync::sync();
         if (n_kept_out) *n_kept_out = 1;
         const int code = sc[12];
-        __syncthreads();
+        Sync::sync();
         return code;
     }
 
@@ -225,15 +239,17 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
     uint32_t low_key = 0;
     if (topk_on) {
         for (int b = tid; b < SAMPLER_BINS; b += SAMPLER_THREADS) hist[b] = 0;
-        __syncthreads();
-        for (int i = tid; i < V; i += SAMPLER_THREADS) atomicAdd(&hist[ord_key(f[i]) >> 21], 1u);
-        __syncthreads();
+        Sync::sync();
+#pragma unroll
+        for (int k = 0; k < NPT; ++k)
+            if (tid + k * SAMPLER_THREADS < V) atomicAdd(&hist[ord_key(fv[k]) >> 21], 1u);
+        Sync::sync();
         // thread t owns descending bins 2047-8t .. 2040-8t
         int s = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) s += (int)hist[SAMPLER_BINS - 1 - (tid * 8 + j)];
         int total;
-        const int before = block_exclusive_scan(s, sc, &total);
+        const int before = block_exclusive_scan<Sync>(s, sc, &total);
         if (before < J.top_k && J.top_k <= before + s) {
             int acc = before;
 #pragma unroll 1
@@ -247,94 +263,121 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
                 acc += h;
             }
         }
-        __syncthreads();
+        Sync::sync();
         low_key = (uint32_t)sc[9] << 21;
     }
-    if (tid == 0) sc[8] = 0;
-    __syncthreads();
-    for (int i = tid; i < V; i += SAMPLER_THREADS) {
-        const uint32_t k = ord_key(f[i]);
-        if (k >= low_key) {
-            const int slot = atomicAdd(&sc[8], 1);
-            cand[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-        }
+    // compaction of every element at or above the cutoff bin: slots come from a
+    // block scan of per-thread counts (the rank sort below fixes the order)
+    int mine = 0;
+#pragma unroll
+    for (int k = 0; k < NPT; ++k)
+        mine += (tid + k * SAMPLER_THREADS < V && ord_key(fv[k]) >= low_key) ? 1 : 0;
+    int C;
+    int slot = block_exclusive_scan<Sync>(mine, sc, &C);
+#pragma unroll
+    for (int k = 0; k < NPT; ++k) {
+        const int i = tid + k * SAMPLER_THREADS;
+        const uint32_t key = ord_key(fv[k]);
+        if (i < V && key >= low_key)
+            cand[slot++] = ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
     }
-    __syncthreads();
-    const int C = sc[8];
+    Sync::sync();
     // exact rank sort, descending by (key, -index)
     for (int i = tid; i < C; i += SAMPLER_THREADS) {
         const unsigned long long ki = cand[i];
         int rank = 0;
+#pragma unroll 4
         for (int j = 0; j < C; ++j) rank += (cand[j] > ki) ? 1 : 0;
         sorted[rank] = ki;
     }
-    __syncthreads();
-    // top-k: keep the sorted prefix with f >= cutoff (ties kept)
+    Sync::sync();
+    // top-k: keep the sorted prefix with f >= cutoff (ties kept); its end is the
+    // one position where f >= cutoff is followed by f < cutoff (or the end)
     int n = C;
     if (topk_on) {
         const float cutoff = key_float((uint32_t)(sorted[J.top_k - 1] >> 32));
-        int cnt = 0;
-        for (int i = tid; i < C; i += SAMPLER_THREADS)
-            cnt += (key_float((uint32_t)(sorted[i] >> 32)) < cutoff) ? 0 : 1;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
-        if ((tid & 31) == 0) sc[16 + (tid >> 5)] = cnt;
-        __syncthreads();
-        if (tid == 0) {
-            int t = 0;
-            for (int w = 0; w < 8; ++w) t += sc[16 + w];
-            sc[10] = t;
+        for (int i = tid; i < C; i += SAMPLER_THREADS) {
+            const bool in = !(key_float((uint32_t)(sorted[i] >> 32)) < cutoff);
+            const bool next_out = (i + 1 == C) || (key_float((uint32_t)(sorted[i + 1] >> 32)) < cutoff);
+            if (in && next_out) sc[10] = i + 1;
         }
-        __syncthreads();
+        Sync::sync();
         n = sc[10];
     }
     const float top = key_float((uint32_t)(sorted[0] >> 32));
     for (int j = tid; j < n; j += SAMPLER_THREADS)
         e[j] = skb_exp(__fsub_rn(key_float((uint32_t)(sorted[j] >> 32)), top));
-    __syncthreads();
-    // sequential FP32 sums in candidate order (thread 0), as the oracle does
+    Sync::sync();
+    // Sequential FP32 sums in candidate order (thread 0), as the oracle does;
+    // operands are read 8 at a time ahead of the dependent adds.
     const bool topp_on = J.top_p > 0.0f && J.top_p < 1.0f;
     if (topp_on) {
         if (tid == 0) {
             float s1 = 0.0f;
-#pragma unroll 8
-            for (int j = 0; j < n; ++j) s1 = __fadd_rn(s1, e[j]);
+            for (int j0 = 0; j0 < n; j0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? e[j0 + t] : 0.f;
+#pragma unroll
+                for (int t = 0; t < 8; ++t)
+                    if (j0 + t < n) s1 = __fadd_rn(s1, v[t]);
+            }
             scf[0] = s1;
         }
-        __syncthreads();
+        Sync::sync();
         const float s1 = scf[0];
         // e_j / S1 in parallel into the candidate area beyond e (floats)
-        float* pj = e + SAMPLER_VMAX;
+        float* pj = e + VMAX;
         for (int j = tid; j < n; j += SAMPLER_THREADS) pj[j] = __fdiv_rn(e[j], s1);
-        __syncthreads();
+        Sync::sync();
         if (tid == 0) {
             // the whole running sum is formed (same adds in the same order as
-            // stopping at the first crossing) so the loads can be pipelined
+            // stopping at the first crossing) so the loads can run ahead
             int keep = n;
             float cum = 0.0f;
-#pragma unroll 8
-            for (int j = 0; j < n; ++j) {
-                cum = __fadd_rn(cum, pj[j]);
-                if (cum > J.top_p && keep == n) keep = j + 1;
+            for (int j0 = 0; j0 < n; j0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? pj[j0 + t] : 0.f;
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    if (j0 + t < n) {
+                        cum = __fadd_rn(cum, v[t]);
+                        if (cum > J.top_p && keep == n) keep = j0 + t + 1;
+                    }
+                }
             }
             sc[11] = keep;
         }
     } else if (tid == 0) {
         sc[11] = n;
     }
-    __syncthreads();
+    Sync::sync();
     if (tid == 0) {
         const int keep = sc[11];
         float s2 = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < keep; ++j) s2 = __fadd_rn(s2, e[j]);
+        for (int j0 = 0; j0 < keep; j0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = (j0 + t < keep) ? e[j0 + t] : 0.f;
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+                if (j0 + t < keep) s2 = __fadd_rn(s2, v[t]);
+        }
         const float t = __fmul_rn(J.u, s2);
         int pick = -1;
         float run = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < keep; ++j) {
-            run = __fadd_rn(run, e[j]);
-            if (run > t && pick < 0) pick = j;
+        for (int j0 = 0; j0 < keep; j0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v[q] = (j0 + q < keep) ? e[j0 + q] : 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (j0 + q < keep) {
+                    run = __fadd_rn(run, v[q]);
+                    if (run > t && pick < 0) pick = j0 + q;
+                }
+            }
         }
         if (pick < 0) {
             pick = 0;
@@ -346,10 +389,10 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         }
         sc[12] = (int)(0xffffffffu - (uint32_t)(sorted[pick] & 0xffffffffull));
     }
-    __syncthreads();
+    Sync::sync();
     if (n_kept_out) *n_kept_out = sc[11];
     const int code = sc[12];
-    __syncthreads();
+    Sync::sync();
     return code;
 }
 

@@ -7,226 +7,15 @@
 
 namespace skb {
 
-// q/k RMSNorm over one head (hd = 128, 4 elements per lane) then neox RoPE.
-// Lane l holds elements [4l, 4l+4); its RoPE partner elements (+-64) live in
-// lane l ^ 16.
-__device__ __forceinline__ float4 norm_rope_head(float4 x, const float* w, float eps,
-                                                 const float* cosr, const float* sinr, int lane,
-                                                 bool do_norm, bool do_rope) {
-    if (do_norm) {
-        float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss / 128.0f + eps);
-        const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + lane);
-        x.x = wv.x * (x.x * inv);
-        x.y = wv.y * (x.y * inv);
-        x.z = wv.z * (x.z * inv);
-        x.w = wv.w * (x.w * inv);
-    }
-    if (do_rope) {
-        float4 o;
-        o.x = __shfl_xor_sync(FULL, x.x, 16);
-        o.y = __shfl_xor_sync(FULL, x.y, 16);
-        o.z = __shfl_xor_sync(FULL, x.z, 16);
-        o.w = __shfl_xor_sync(FULL, x.w, 16);
-        const int i0 = (lane & 15) * 4;  // frequency index of element 0
-        const float4 c = *reinterpret_cast<const float4*>(cosr + i0);
-        const float4 s = *reinterpret_cast<const float4*>(sinr + i0);
-        if (lane < 16) {  // first half: x*cos - x[i+64]*sin
-            x.x = x.x * c.x - o.x * s.x;
-            x.y = x.y * c.y - o.y * s.y;
-            x.z = x.z * c.z - o.z * s.z;
-            x.w = x.w * c.w - o.w * s.w;
-        } else {  // second half: x*cos + x[i-64]*sin
-            x.x = x.x * c.x + o.x * s.x;
-            x.y = x.y * c.y + o.y * s.y;
-            x.z = x.z * c.z + o.z * s.z;
-            x.w = x.w * c.w + o.w * s.w;
-        }
-    }
-    return x;
-}
-
-// grid (S, KVH, R), 256 threads.  CTA (s, g, r) owns positions
-// [s*T/S, (s+1)*T/S) of row r's cache for kv head g (T = cached length + 1).
-// Warp w takes positions pb+w, pb+w+8, ... in batches of 4: the K and V rows of
-// a batch (512 B each, one float4 per lane) are loaded together, scores are
-// warp-reduced, and an online softmax keeps (max, sum, o[h][lane*4..+4]) per
-// warp.  The 8 warps merge through shared memory into the CTA's partial; the
-// last CTA of each (row, kv head) -- an atomic ticket, no waiting -- merges the
-// S partials in split order and writes the attention output.
-constexpr int ATT_B = 4;
-
+// grid (S, KVH, R), 256 threads: one work item per CTA.
 __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a) {
-    __shared__ __align__(16) float qs[2][128];
-    __shared__ __align__(16) float ks[128];
-    __shared__ __align__(16) float vs[128];
-    __shared__ __align__(16) float wo[8][2][128];
-    __shared__ float wm[8][2], wl[8][2];
-    __shared__ int sm_last;
-
+    __shared__ AttnSmem sm;
     const int s = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nblk = gridDim.x * gridDim.y * gridDim.z;
     prefetch_share(a.pf, (r * gridDim.y + g) * gridDim.x + s, nblk);
     pdl_wait();
     pdl_trigger();
-
-    int p_new = a.pos[r];
-    if (p_new < 0 || p_new >= a.max_len) {
-        if (tid == 0 && a.err != nullptr) atomicExch(a.err, 1);
-        p_new = p_new < 0 ? 0 : a.max_len - 1;
-    }
-    const int T = p_new + 1;
-    const float* row = a.qkv + (size_t)r * a.ld_qkv;
-    const float* cosr = a.rope_cos + (size_t)p_new * 64;
-    const float* sinr = a.rope_sin + (size_t)p_new * 64;
-    const int n_rep = a.n_rep;
-    if (warp == 0) {
-        float4 k = ld_cg4(reinterpret_cast<const float4*>(row + (a.H + g) * 128) + lane);
-        k = norm_rope_head(k, a.kn, a.eps, cosr, sinr, lane, true, true);
-        reinterpret_cast<float4*>(ks)[lane] = k;
-    } else if (warp <= n_rep) {
-        const int h = g * n_rep + (warp - 1);
-        float4 q = ld_cg4(reinterpret_cast<const float4*>(row + h * 128) + lane);
-        q = norm_rope_head(q, a.qn, a.eps, cosr, sinr, lane, true, true);
-        q.x *= a.scale;
-        q.y *= a.scale;
-        q.z *= a.scale;
-        q.w *= a.scale;
-        reinterpret_cast<float4*>(qs[warp - 1])[lane] = q;
-    } else if (warp == n_rep + 1) {
-        const float4 v =
-            ld_cg4(reinterpret_cast<const float4*>(row + (a.H + a.kv.KVH + g) * 128) + lane);
-        reinterpret_cast<float4*>(vs)[lane] = v;
-    }
-    __syncthreads();
-
-    const int pb = (int)((long long)s * T / a.S);
-    const int pe = (int)((long long)(s + 1) * T / a.S);
-    if (s == a.S - 1 && tid < 128) {
-        a.kv.at(a.layer, r, p_new, 0, g)[tid] = ks[tid];
-        a.kv.at(a.layer, r, p_new, 1, g)[tid] = vs[tid];
-    }
-    float4 q4[2];
-    q4[0] = reinterpret_cast<const float4*>(qs[0])[lane];
-    q4[1] = n_rep > 1 ? reinterpret_cast<const float4*>(qs[1])[lane] : q4[0];
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    float4 o[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-    for (int p0 = pb + warp; p0 < pe; p0 += 8 * ATT_B) {
-        float4 kb[ATT_B], vb[ATT_B];
-#pragma unroll
-        for (int j = 0; j < ATT_B; ++j) {
-            const int p = p0 + 8 * j;
-            if (p < pe) {
-                if (p == p_new) {
-                    kb[j] = reinterpret_cast<const float4*>(ks)[lane];
-                    vb[j] = reinterpret_cast<const float4*>(vs)[lane];
-                } else {
-                    kb[j] = ld_cg4(reinterpret_cast<const float4*>(a.kv.at(a.layer, r, p, 0, g)) + lane);
-                    vb[j] = ld_cg4(reinterpret_cast<const float4*>(a.kv.at(a.layer, r, p, 1, g)) + lane);
-                }
-            } else {
-                kb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                vb[j] = kb[j];
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            if (h >= n_rep) break;
-            float sc[ATT_B];
-#pragma unroll
-            for (int j = 0; j < ATT_B; ++j) {
-                float d = q4[h].x * kb[j].x + q4[h].y * kb[j].y + q4[h].z * kb[j].z + q4[h].w * kb[j].w;
-                d = warp_sum(d);
-                sc[j] = (p0 + 8 * j < pe) ? d : -INFINITY;
-            }
-            float mt = sc[0];
-#pragma unroll
-            for (int j = 1; j < ATT_B; ++j) mt = fmaxf(mt, sc[j]);
-            const float mn = fmaxf(m[h], mt);
-            const float corr = expf(m[h] - mn);
-            float lsum = l[h] * corr;
-            float4 acc = make_float4(o[h].x * corr, o[h].y * corr, o[h].z * corr, o[h].w * corr);
-#pragma unroll
-            for (int j = 0; j < ATT_B; ++j) {
-                const float e = expf(sc[j] - mn);
-                lsum += e;
-                acc.x = fmaf(e, vb[j].x, acc.x);
-                acc.y = fmaf(e, vb[j].y, acc.y);
-                acc.z = fmaf(e, vb[j].z, acc.z);
-                acc.w = fmaf(e, vb[j].w, acc.w);
-            }
-            m[h] = mn;
-            l[h] = lsum;
-            o[h] = acc;
-        }
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        if (h >= n_rep) break;
-        reinterpret_cast<float4*>(wo[warp][h])[lane] = o[h];
-        if (lane == 0) {
-            wm[warp][h] = m[h];
-            wl[warp][h] = l[h];
-        }
-    }
-    __syncthreads();
-    const int hd2 = 128 + 2;
-    float* part = a.part + ((((size_t)r * a.kv.KVH + g) * a.S + s) * n_rep) * hd2;
-    if (tid < n_rep * 128) {
-        const int h = tid >> 7, d = tid & 127;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w][h]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                const float c = expf(wm[w][h] - M);
-                L = fmaf(wl[w][h], c, L);
-                O = fmaf(wo[w][h][d], c, O);
-            }
-        }
-        part[h * hd2 + d] = O;
-        if (d == 0) {
-            part[h * hd2 + 128] = M;
-            part[h * hd2 + 129] = L;
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) sm_last = (atomicAdd(&a.counters[r * a.kv.KVH + g], 1) == a.S - 1) ? 1 : 0;
-    __syncthreads();
-    if (!sm_last) return;
-    __threadfence();
-    // Merge the S split partials in split order.  The (max, sum) pairs are
-    // staged in shared memory by parallel loads first, so the weighted sum over
-    // the splits issues its partial-output loads independently of each other.
-    {
-        const float* base = a.part + ((((size_t)r * a.kv.KVH + g) * a.S) * n_rep) * hd2;
-        float* sm_ml = &wo[0][0][0];  // reuse: [S][n_rep][2] (S * 4 floats <= 2048)
-        for (int i = tid; i < a.S * n_rep; i += 256) {
-            sm_ml[2 * i] = __ldcg(base + (size_t)i * hd2 + 128);
-            sm_ml[2 * i + 1] = __ldcg(base + (size_t)i * hd2 + 129);
-        }
-        __syncthreads();
-        if (tid < n_rep * 128) {
-            const int h = tid >> 7, d = tid & 127;
-            float M = -INFINITY;
-            for (int j = 0; j < a.S; ++j) M = fmaxf(M, sm_ml[2 * (j * n_rep + h)]);
-            float L = 0.f, O = 0.f;
-#pragma unroll 8
-            for (int j = 0; j < a.S; ++j) {
-                const float mj = sm_ml[2 * (j * n_rep + h)];
-                const float w = (mj == -INFINITY) ? 0.f : expf(mj - M);
-                L = fmaf(sm_ml[2 * (j * n_rep + h) + 1], w, L);
-                O = fmaf(__ldcg(base + ((size_t)j * n_rep + h) * hd2 + d), w, O);
-            }
-            a.out[(size_t)r * a.H * 128 + (g * n_rep + h) * 128 + d] = O / L;
-        }
-    }
-    if (tid == 0) a.counters[r * a.kv.KVH + g] = 0;
+    decode_attn_item<BlockSync>(a, s, g, r, sm);
 }
 
 cudaError_t decode_attn_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl) {

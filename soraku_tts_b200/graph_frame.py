@@ -16,7 +16,9 @@ Differences from the reference, all semantics-preserving:
   ``torch.multinomial``; greedy decoding (``sampled=False``) is argmax as in
   the reference;
 * ``top_k``/``top_p`` are runtime parameters, so changing them needs no
-  recapture.
+  recapture;
+* ``persistent=True`` records each frame chunk as one persistent cooperative
+  kernel instead of the separate-kernel sequence.
 """
 
 from __future__ import annotations
@@ -40,11 +42,12 @@ class NativeEngine:
     """Thin owner of an ``skb_engine*`` (the C ABI of include/soraku_b200.h)."""
 
     def __init__(self, model, *, max_requests=1, rows_per_request=2, max_len=1024, max_frames=1024,
-                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True):
+                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True,
+                 persistent=False):
         self.model = model
         opts = _lib.skb_engine_opts(max_requests, rows_per_request, max_len, max_frames,
                                     max_prefill if max_prefill else max_len, page_size, attn_splits,
-                                    1 if use_pdl else 0, 1 if l2_prefetch else 0)
+                                    1 if use_pdl else 0, 1 if l2_prefetch else 0, 1 if persistent else 0)
         handle = ctypes.c_void_p()
         desc = model.model_desc()
         _lib.call("skb_engine_create", ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
@@ -101,10 +104,15 @@ class NativeEngine:
     def frames(self, request=0) -> int:
         return int(_lib.lib().skb_engine_frames(self.h, request))
 
-    def read_codes(self, request, first, n, out=None, stream=None) -> torch.Tensor:
+    def read_codes(self, request, first, n, out=None, stream=None, sync=True) -> torch.Tensor:
+        """Codes [n, Q] of frames first..first+n-1.  The copy is asynchronous on
+        the stream; with sync=True (default) the stream is synchronised before
+        returning, so the host buffer holds the codes."""
         if out is None:
             out = torch.empty((n, self.Q), dtype=torch.int64, pin_memory=True)
         _lib.call("skb_engine_read_codes", self.h, request, first, n, out.data_ptr(), _lib.stream_ptr(stream))
+        if sync:
+            (torch.cuda.current_stream() if stream is None else stream).synchronize()
         return out
 
     def view(self, which: int, dtype=torch.float32) -> torch.Tensor:
@@ -118,6 +126,13 @@ class NativeEngine:
 
     def kernels_per_frame(self) -> int:
         return int(_lib.lib().skb_engine_kernels_per_frame(self.h))
+
+    def launches_per_step(self) -> int:
+        """Kernel launches of one step() of the captured graph."""
+        return int(_lib.lib().skb_engine_launches_per_step(self.h))
+
+    def is_persistent(self) -> bool:
+        return bool(_lib.lib().skb_engine_is_persistent(self.h))
 
 
 def _host_ids(ids) -> torch.Tensor:
@@ -142,7 +157,7 @@ class GraphFrameEngine:
 
     def __init__(self, model, *, device: torch.device, max_cache_len: int, cfg_scale: float = 1.5,
                  batch: int = 2, max_frames: int | None = None, use_pdl: bool = True,
-                 l2_prefetch: bool = True) -> None:
+                 l2_prefetch: bool = True, persistent: bool = False) -> None:
         if batch not in (1, 2):
             raise ValueError("batch must be 1 (no CFG) or 2 (cond + uncond)")
         self.model = as_soraku_model(model, device)
@@ -155,7 +170,7 @@ class GraphFrameEngine:
         self.max_len = int(max_cache_len)
         self.native = NativeEngine(self.model, max_requests=1, rows_per_request=batch, max_len=self.max_len,
                                    max_frames=max_frames or self.max_len, max_prefill=self.max_len,
-                                   use_pdl=use_pdl, l2_prefetch=l2_prefetch)
+                                   use_pdl=use_pdl, l2_prefetch=l2_prefetch, persistent=persistent)
         self.cfg = torch.tensor([cfg_scale], device=self.device, dtype=torch.float32)
         self.graph = None
         self.top_k: int | None = None
