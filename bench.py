@@ -66,7 +66,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true")
-    ap.add_argument("--persistent", action="store_true", help="run frames as the persistent frame kernel")
+    ap.add_argument("--kernel-only", action="store_true", help="time only the dominant kernel (for ncu captures)")
     return ap.parse_args()
 
 
@@ -138,6 +138,79 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
+
+
+GATEUP_PROFILE = os.path.join(HERE, "profiles", "gemv_swiglu_m2_trunk_gateup.md")
+
+
+def time_gateup_kernel(params, n_layers: int, reps: int = 10):
+    """The dominant decode kernel timed alone: the trunk gate/up SwiGLU GEMV
+    (M = 2 CFG rows, 2 x 3072 x 1024 FP32 weights) over every layer's weights
+    back to back (28 x 25.2 MB, far more than L2), recorded as a CUDA graph so
+    host launch overhead stays out of the CUDA-event timing.  Returns (ms per
+    launch, algorithmic bytes per launch)."""
+    import torch
+
+    from soraku_tts_b200 import kernels as K
+
+    x = torch.randn(2, 1024, device="cuda")
+    k_su = K.swiglu_gemv(2, 3072, 1024)
+    layers = [(params[f"trunk.layers.{i}.mlp.gate_proj.weight"], params[f"trunk.layers.{i}.mlp.up_proj.weight"])
+              for i in range(n_layers)]
+    for wg, wu in layers:
+        k_su(x, wg, wu)
+    torch.cuda.synchronize()
+    kgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(kgraph):
+        for wg, wu in layers:
+            k_su(x, wg, wu)
+    kgraph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ka.record(stream)
+    for _ in range(reps):
+        kgraph.replay()
+    kb.record(stream)
+    torch.cuda.synchronize()
+    k_ms = ka.elapsed_time(kb) / (reps * len(layers))
+    del kgraph
+    k_bytes = 2 * 3072 * 1024 * 4 + 2 * 1024 * 4 + 2 * 3072 * 4
+    return k_ms, k_bytes
+
+
+def profiled_traffic():
+    """DRAM bytes (read + write) per launch of the gate/up GEMV from the
+    committed ncu summary (its line 'dram_bytes_per_launch: N'), else None."""
+    try:
+        with open(GATEUP_PROFILE) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].strip().replace(",", ""))
+    except OSError:
+        pass
+    return None
+
+
+def kernel_only_main(args):
+    """--kernel-only: just the dominant kernel's timing on random weights of
+    the trunk's gate/up shape (a small command for ncu captures)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    n_layers = 28
+    g = torch.Generator(device="cuda")
+    g.manual_seed(42)
+    params = {}
+    for i in range(n_layers):
+        for nm in ("gate_proj", "up_proj"):
+            params[f"trunk.layers.{i}.mlp.{nm}.weight"] = torch.randn(3072, 1024, device="cuda", generator=g) * 0.02
+    k_ms, k_bytes = time_gateup_kernel(params, n_layers)
+    peak, peak_kind = measured_peak_hbm()
+    gbs = k_bytes / (k_ms * 1e-3) / 1e9
+    print(json.dumps({"kernel": "gemv_kernel swiglu M=2 3072x1024", "launch_ms": round(k_ms, 5),
+                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_kind": peak_kind}), flush=True)
+    return 0
 
 
 # ----------------------------------------------------------------- reference
@@ -222,8 +295,7 @@ def b200_main(args, wl):
     model = SorakuModel.random(dims, 42, f"cuda:{local}")
     weights_bytes = sum(t.numel() * 4 for k, t in model.params.items() if k != "trunk.embed_tokens.weight")
     gen = FastGenerator(model, device=torch.device("cuda", local), frames_per_graph=fpg,
-                        use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch,
-                        persistent=args.persistent)
+                        use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch)
     ids, uncond, prompt = make_inputs(1000 + rank, wl["n_text"], wl["n_ref"])
     gkw = dict(max_new_frames=frames, min_new_frames=frames, **SAMPLING)
 
@@ -286,34 +358,7 @@ def b200_main(args, wl):
     h2d = int(ids.nbytes + uncond.nbytes + prompt.nbytes)
     d2h = int(frames * 16 * 8)
 
-    # ---- dominant kernel, timed alone: the trunk gate/up GEMV (M = 2 CFG rows,
-    # 3072 x 2 x 1024 FP32 weights) over all 28 layers' weights back to back
-    from soraku_tts_b200 import kernels as K
-
-    x = torch.randn(2, 1024, device="cuda")
-    k_su = K.swiglu_gemv(2, 3072, 1024)
-    layers = [(model.params[f"trunk.layers.{i}.mlp.gate_proj.weight"], model.params[f"trunk.layers.{i}.mlp.up_proj.weight"])
-              for i in range(dims.trunk.num_hidden_layers)]
-    for wg, wu in layers:
-        k_su(x, wg, wu)
-    torch.cuda.synchronize()
-    # record the 28 launches as a CUDA graph so host launch overhead stays out of the timing
-    kgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(kgraph):
-        for wg, wu in layers:
-            k_su(x, wg, wu)
-    kgraph.replay()
-    torch.cuda.synchronize()
-    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 10
-    ka.record(stream)
-    for _ in range(reps):
-        kgraph.replay()
-    kb.record(stream)
-    torch.cuda.synchronize()
-    k_ms = ka.elapsed_time(kb) / (reps * len(layers))
-    del kgraph
-    k_bytes = 2 * 3072 * 1024 * 4 + 2 * 1024 * 4 + 2 * 3072 * 4
+    k_ms, k_bytes = time_gateup_kernel(model.params, dims.trunk.num_hidden_layers)
     peak, peak_kind = measured_peak_hbm()
     k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
     bpf = bytes_per_frame(weights_bytes, wl["n_text"], wl["n_ref"], frames)
@@ -347,14 +392,13 @@ def b200_main(args, wl):
             "global_batch": world, "rows_per_gpu": 2, "seq_len": 2 + wl["n_text"] + wl["n_ref"] + frames,
             "parallelism": "replicas" if world > 1 else "single",
             "frames_per_graph": fpg, "pdl": not args.no_pdl, "l2_prefetch": not args.no_prefetch,
-            "persistent_kernel": eng.is_persistent(),
             "rtf": round(FRAME_RATE / (value / world), 5), "prefill_ms": round(statistics.mean(pre_ms), 2),
             "frame_ms": round(frame_ms, 4), "l2": "inputs larger than L2: each frame streams ~2.1 GB",
             "wall_s_value_region": round(t_wall, 3),
         },
         "e2e": {"value": round(e2e, 3), "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(k_gbs / peak, 4), "traffic": None,
+                     "frac": round(k_gbs / peak, 4), "traffic": profiled_traffic(),
                      "kernel": "gemv_kernel (trunk gate/up SwiGLU GEMV, M=2, 25.2 MB weights/launch)",
                      "peak_kind": peak_kind, "launch_ms": round(k_ms, 5), "bytes_per_launch": k_bytes},
         "roofline_frame": {"bound": "hbm", "achieved": round(f_gbs, 1), "peak": peak, "unit": "GB/s",
@@ -373,6 +417,8 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return reference_main(args, wl)
+    if args.kernel_only:
+        return kernel_only_main(args)
     return b200_main(args, wl)
 
 

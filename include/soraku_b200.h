@@ -208,9 +208,6 @@ typedef struct {
     int attn_splits;      /* 0 = choose; KV splits per (row, kv head)      */
     int use_pdl;          /* programmatic dependent launch between kernels */
     int l2_prefetch;      /* bulk-prefetch the next kernel's weights       */
-    int persistent;       /* run frames as one persistent cooperative kernel
-                             (falls back to separate kernels when the model's
-                             shapes do not fit it)                          */
 } skb_engine_opts;
 
 int skb_engine_create(const skb_model_desc *model, const skb_engine_opts *opts, skb_engine **out);
@@ -257,22 +254,18 @@ int skb_engine_frames(skb_engine *eng, int request);
 /* Device views of engine state for tests: which = 0 x (residual stream)
  * [R, d]; 1 hidden [R, d]; 2 logits [R, V] of the last depth step; 3 pos
  * int32 [R]; 4 logits history [Q, R, V] of the last frame (debug capture must
- * be on); 5 prefix [n_req, d]; 6 error flags int32 [8]; 7 request state;
- * 8 persistent-kernel phase timeline uint64 [frames, phases, 2] (debug on);
- * 9 per-CTA phase end stamps uint64 [frames <= 8, phases, SMs] (debug on). */
+ * be on); 5 prefix [n_req, d]; 6 error flags int32 [8]; 7 request state. */
 int skb_engine_view(skb_engine *eng, int which, void **ptr, int64_t *numel);
 
 /* Keep the per-(q) logits of the last frame in the history buffer (view 4). */
 int skb_engine_set_debug(skb_engine *eng, int on);
 
-/* Number of kernels one frame launches on the separate-kernel path. */
+/* Number of kernels one frame launches. */
 int skb_engine_kernels_per_frame(skb_engine *eng);
 
 /* Kernel launches one skb_engine_step makes with the captured graph
- * (frames_per_graph x kernels per frame, or 1 for the persistent kernel),
- * and whether that graph runs the persistent kernel (1) or not (0). */
+ * (frames_per_graph x kernels per frame; 0 before capture). */
 int skb_engine_launches_per_step(skb_engine *eng);
-int skb_engine_is_persistent(skb_engine *eng);
 
 #ifdef __cplusplus
 }

@@ -56,7 +56,6 @@ SIGNATURES = {
     "skb_engine_set_debug": (c_int, [c_void_p, c_int]),
     "skb_engine_kernels_per_frame": (c_int, [c_void_p]),
     "skb_engine_launches_per_step": (c_int, [c_void_p]),
-    "skb_engine_is_persistent": (c_int, [c_void_p]),
 }
 
 
@@ -85,7 +84,7 @@ class skb_model_desc(ctypes.Structure):
 class skb_engine_opts(ctypes.Structure):
     _fields_ = [("max_requests", c_int), ("rows_per_request", c_int), ("max_len", c_int),
                 ("max_frames", c_int), ("max_prefill", c_int), ("page_size", c_int),
-                ("attn_splits", c_int), ("use_pdl", c_int), ("l2_prefetch", c_int), ("persistent", c_int)]
+                ("attn_splits", c_int), ("use_pdl", c_int), ("l2_prefetch", c_int)]
 
 
 _lib = None

@@ -40,8 +40,9 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, unsigned bytes) 
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ void prefetch_share(const PrefetchList& pf, int cta, int ncta) {
-    if (threadIdx.x != 0 || pf.n <= 0) return;
+// Issued by the calling thread alone.
+__device__ __forceinline__ void prefetch_share_from(const PrefetchList& pf, int cta, int ncta) {
+    if (pf.n <= 0) return;
     unsigned long long total = 0;
     for (int i = 0; i < pf.n; ++i) total += pf.bytes[i] & ~15ull;
     // 16-byte granules keep every prefetch aligned
@@ -64,6 +65,11 @@ __device__ __forceinline__ void prefetch_share(const PrefetchList& pf, int cta, 
             a += chunk;
         }
     }
+}
+
+// Issued by thread 0 of the CTA.
+__device__ __forceinline__ void prefetch_share(const PrefetchList& pf, int cta, int ncta) {
+    if (threadIdx.x == 0) prefetch_share_from(pf, cta, ncta);
 }
 
 // ----------------------------------------------------------- vector loads
@@ -125,25 +131,10 @@ __device__ __forceinline__ float butterfly_reduce(float (&v)[N], int lane) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
-// Barrier policies for code shared by standalone kernels (every thread of the
-// CTA takes part) and the persistent frame kernel (only its 256 consumer
-// threads take part; the producer warp runs independently).
+// Barrier policy of the block-wide building blocks (sampler, attention item):
+// every thread of the CTA takes part.
 struct BlockSync {
     __device__ __forceinline__ static void sync() { __syncthreads(); }
-};
-struct ConsumerSync {
-    __device__ __forceinline__ static void sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-    // Barrier that also returns the AND of `p` over the 256 consumer threads,
-    // so a decision taken per thread becomes uniform.
-    __device__ __forceinline__ static bool sync_and(bool p) {
-        int r;
-        asm volatile(
-            "{\n .reg .pred a, b;\n setp.ne.s32 a, %1, 0;\n bar.red.and.pred b, 1, 256, a;\n selp.s32 %0, 1, 0, b;\n}\n"
-            : "=r"(r)
-            : "r"((int)p)
-            : "memory");
-        return r != 0;
-    }
 };
 
 // ------------------------------------------------------ bulk copy + mbarrier

@@ -27,7 +27,7 @@
 #include <vector>
 
 #include "engine_types.cuh"
-#include "frame.cuh"
+#include "trunk.cuh"
 #include "ops.cuh"
 #include "sampler.cuh"
 #include "trunk_api.cuh"
@@ -77,19 +77,23 @@ struct skb_engine {
     std::vector<int> frames_host, pos_host;
     std::vector<ReqState> st_host;
     std::vector<void*> allocs;
-    // persistent frame kernel
-    Phase* d_prog = nullptr;
-    int max_prog = 0;
-    unsigned* bar_count = nullptr;
-    int graph_persistent = 0;  // the captured step runs the persistent kernel
-    int persistent_direct = 0; // ... launched directly (the graph capture was refused)
-    FrameArgs fargs = {};
-    int fk_M = 0;
-    unsigned long long* timeline = nullptr;  // persistent-kernel phase timestamps (debug)
-    unsigned long long* cta_end = nullptr;   // per-CTA phase end stamps (debug, up to 8 frames)
 };
 
 namespace {
+
+enum : int { PH_GEMV = 0, PH_ATTN = 1 };
+
+// One step of the frame program: a GEMV launch (whose classifier step may
+// carry the depth sampler that follows it) or a decode-attention launch.
+struct Phase {
+    int kind;
+    int xm, em;
+    int sample;
+    int n_req;
+    GemvArgs g;
+    DepthSampleArgs s;
+    DecodeAttnArgs at;
+};
 
 template <typename T>
 int dalloc(skb_engine* e, T** p, size_t n) {
@@ -170,14 +174,12 @@ Phase gemv_phase(const GemvArgs& a, int XM, int EM) {
     ph.kind = PH_GEMV;
     ph.xm = XM;
     ph.em = EM;
-    ph.kv4 = ((a.K >> 2) + GEMV_THREADS - 1) / GEMV_THREADS;
     ph.g = a;
     return ph;
 }
 
-// The frame as a program of phases (16 depth steps, then the trunk layers).
-// Both execution paths are built from it: separate kernels chained with PDL
-// (build_frame) or the persistent frame kernel (the program uploaded as is).
+// The frame as a program of phases (16 depth steps, then the trunk layers),
+// turned into kernel launches chained with PDL by build_frame.
 std::vector<Phase> build_phases(skb_engine* e, int n_active) {
     std::vector<Phase> phases;
     const int R = n_active * e->rpr;
@@ -286,7 +288,6 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
             a.err = e->err;
             Phase ph = {};
             ph.kind = PH_ATTN;
-            ph.attn_rows = R;
             ph.at = a;
             phases.push_back(ph);
         }
@@ -406,30 +407,6 @@ void destroy_graph(skb_engine* e) {
     e->exec = nullptr;
     e->graph_active = 0;
     e->graph_fpg = 0;
-    e->graph_persistent = 0;
-    e->persistent_direct = 0;
-}
-
-// The persistent kernel serves a model when every GEMV phase's inner size is
-// 1024, 2048 or 3072 (the ring-slot chunking it is compiled for), the CFG rows
-// are 1, 2 or 4, the audio vocabulary fits its sampler, and one CTA fits per SM.
-bool persistent_fits(const skb_engine* e, const std::vector<Phase>& phases, int R) {
-    if (R != 1 && R != 2 && R != 4) return false;
-    if (e->V > FK_VMAX) return false;
-    if ((int)phases.size() > e->max_prog) return false;
-    for (const Phase& ph : phases)
-        if (ph.kind == PH_GEMV && (ph.g.K % 1024 != 0 || ph.g.K > 3072)) return false;
-    if (frame_kernel_prepare(R) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    return frame_kernel_occupancy(R) >= 1;
-}
-
-int launch_persistent(skb_engine* e, cudaStream_t s) {
-    cudaError_t err = cudaMemsetAsync(e->bar_count, 0, sizeof(unsigned), s);
-    if (err == cudaSuccess) err = frame_kernel_launch(e->fk_M, e->fargs, e->nsm, s);
-    return err == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "persistent frame kernel: %s", cudaGetErrorString(err));
 }
 
 int upload_state(skb_engine* e, int req, cudaStream_t s) {
@@ -531,7 +508,6 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->counters, (size_t)e->R * e->KVH)
     A(e->page_table, (size_t)e->R * e->max_pages)
     A(e->err, 8)
-    A(e->bar_count, 1)
     A(e->host_flag, 1)
     A(e->cur_codes, (size_t)e->nreq * e->Q)
     A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
@@ -547,10 +523,6 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->ptok, T)
     A(e->pframes, (size_t)(opts->max_prefill + 1) * e->Q)
     A(e->pmeta, 5 * 8)
-    e->max_prog = e->Q * 3 + e->L * 5;
-    A(e->d_prog, e->max_prog)
-    A(e->timeline, (size_t)64 * e->max_prog * 2)
-    A(e->cta_end, (size_t)8 * e->max_prog * e->nsm)
 #undef A
     if (st != SKB_OK) {
         skb_engine_destroy(e);
@@ -802,42 +774,6 @@ int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream
     cudaStream_t cs = e->cap_stream;
     cudaError_t err = cudaStreamSynchronize(stream);
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "capture sync: %s", cudaGetErrorString(err));
-    if (e->o.persistent) {
-        const std::vector<Phase> phases = build_phases(e, n_active);
-        const int R = n_active * e->rpr;
-        if (persistent_fits(e, phases, R)) {
-            err = cudaMemcpy(e->d_prog, phases.data(), sizeof(Phase) * phases.size(), cudaMemcpyHostToDevice);
-            if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "program upload: %s", cudaGetErrorString(err));
-            e->fk_M = R;
-            e->fargs.prog = e->d_prog;
-            e->fargs.n_phases = (int)phases.size();
-            e->fargs.frames = fpg;
-            e->fargs.bar_count = e->bar_count;
-            e->fargs.abort_flag = e->err + 4;
-            e->fargs.err = e->err;
-            e->fargs.sample_ticket = e->err + 5;
-            e->fargs.timeline = e->debug ? e->timeline : nullptr;
-            e->fargs.cta_end = (e->debug && fpg <= 8) ? e->cta_end : nullptr;
-            e->graph_active = n_active;
-            e->graph_fpg = fpg;
-            e->graph_persistent = 1;
-            cudaGraph_t graph = nullptr;
-            err = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
-            int st = err == cudaSuccess ? launch_persistent(e, cs) : SKB_ERR_CUDA;
-            cudaError_t end = err == cudaSuccess ? cudaStreamEndCapture(cs, &graph) : err;
-            if (st == SKB_OK && end == cudaSuccess && graph &&
-                cudaGraphInstantiate(&e->exec, graph, 0) == cudaSuccess) {
-                cudaGraphDestroy(graph);
-                return SKB_OK;
-            }
-            // the cooperative launch could not be recorded: launch it directly per step
-            cudaGetLastError();
-            if (graph) cudaGraphDestroy(graph);
-            e->exec = nullptr;
-            e->persistent_direct = 1;
-            return SKB_OK;
-        }
-    }
     const std::vector<Node> nodes = build_frame(e, n_active);
     for (int attempt = 0; attempt < 2; ++attempt) {
         const bool pdl = e->o.use_pdl && attempt == 0;
@@ -890,20 +826,13 @@ static void advance_host(skb_engine* e, int n_active, int frames) {
 
 int skb_engine_step(skb_engine* e, int mask_eos_q0, cudaStream_t stream) {
     if (!e) return fail(SKB_ERR_ARG, "step: null engine");
-    if (!e->exec && !e->persistent_direct) return fail(SKB_ERR_STATE, "call capture() first");
+    if (!e->exec) return fail(SKB_ERR_STATE, "call capture() first");
     int st = check_capacity(e, e->graph_active, e->graph_fpg);
     if (st) return st;
     static thread_local int flag_val;
     flag_val = mask_eos_q0 ? 1 : 0;
     cudaError_t err = cudaMemcpyAsync(e->host_flag, &flag_val, sizeof(int), cudaMemcpyHostToDevice, stream);
-    if (err == cudaSuccess) {
-        if (e->persistent_direct) {
-            st = launch_persistent(e, stream);
-            if (st) return st;
-        } else {
-            err = cudaGraphLaunch(e->exec, stream);
-        }
-    }
+    if (err == cudaSuccess) err = cudaGraphLaunch(e->exec, stream);
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "step: %s", cudaGetErrorString(err));
     advance_host(e, e->graph_active, e->graph_fpg);
     return SKB_OK;
@@ -949,8 +878,6 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
         case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
-        case 8: *ptr = e->timeline; *numel = (int64_t)64 * e->max_prog * 2; break;
-        case 9: *ptr = e->cta_end; *numel = (int64_t)8 * e->max_prog * e->nsm; break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }
     return SKB_OK;
@@ -970,10 +897,8 @@ int skb_engine_kernels_per_frame(skb_engine* e) {
 
 int skb_engine_launches_per_step(skb_engine* e) {
     if (!e) return -1;
-    if (!e->exec && !e->persistent_direct) return 0;
-    return e->graph_persistent ? 1 : e->graph_fpg * skb_engine_kernels_per_frame(e);
+    if (!e->exec) return 0;
+    return e->graph_fpg * skb_engine_kernels_per_frame(e);
 }
-
-int skb_engine_is_persistent(skb_engine* e) { return e ? e->graph_persistent : -1; }
 
 }  // extern "C"

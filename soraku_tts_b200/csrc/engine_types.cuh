@@ -1,5 +1,4 @@
-// Engine state shared by the multi-kernel frame and the persistent frame
-// kernel: per-request sampling state and the depth-sampler step.
+// Engine state: per-request sampling state and the depth-sampler step.
 #pragma once
 
 #include "common.cuh"

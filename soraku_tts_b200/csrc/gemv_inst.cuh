@@ -1,6 +1,8 @@
-// Instantiation of gemv_kernel for one activation-row count (GEMV_M), over
-// the (prologue, epilogue) pairs the engine and the op surface use.
+// Instantiation of the ring-streamed decode GEMV (rgemv_kernel) for one
+// activation-row count (GEMV_M), over the inner sizes K <= 1024, 2048, 3072
+// and the (prologue, epilogue) pairs the engine and the op surface use.
 #include "ops.cuh"
+#include "rgemv.cuh"
 
 #ifndef GEMV_M
 #error "define GEMV_M"
@@ -11,19 +13,20 @@
 
 namespace skb {
 
-template <int KV4, int XMV, int EMV>
-static cudaError_t gemv_go(const GemvArgs& a, int grid, cudaStream_t s, bool pdl) {
-    auto kern = gemv_kernel<GEMV_M, KV4, XMV, EMV>;
-    if (grid <= 0)  // prepare only
-        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_MAX);
-    const int G = gemv_grid(a.N, a.K, EMV, grid, GemvShape<GEMV_M, KV4>::RC);
-    return launch(kern, dim3(G), dim3(GEMV_THREADS), gemv_smem_bytes(a.N, a.K, EMV, G), s, pdl, a);
+template <int KQ, int XMV, int EMV>
+static cudaError_t gemv_go(const GemvArgs& a, const RgPlan& p, cudaStream_t s, bool pdl) {
+    constexpr bool XR = (KQ == 8 && GEMV_M <= 2);
+    auto kern = rgemv_kernel<GEMV_M, KQ, XMV, EMV, XR>;
+    if (p.grid <= 0)  // prepare only
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RG_SMEM_BUDGET);
+    return launch(kern, dim3(p.grid), dim3(RG_THREADS), p.smem, s, pdl, a, p.slots);
 }
 
-template <int KV4>
-static cudaError_t gemv_dispatch_em(const GemvArgs& a, int XM, int EM, int grid, cudaStream_t s, bool pdl) {
-#define SKB_CASE(XMV, EMV)                                                                       \
-    if (XM == XMV && EM == EMV) return gemv_go<KV4, XMV, EMV>(a, grid, s, pdl);
+template <int KQ>
+static cudaError_t gemv_dispatch_em(const GemvArgs& a, int XM, int EM, const RgPlan& p, cudaStream_t s,
+                                    bool pdl) {
+#define SKB_CASE(XMV, EMV) \
+    if (XM == XMV && EM == EMV) return gemv_go<KQ, XMV, EMV>(a, p, s, pdl);
     SKB_CASE(X_PLAIN, E_STORE)
     SKB_CASE(X_PLAIN, E_RESID)
     SKB_CASE(X_PLAIN, E_BIAS)
@@ -37,28 +40,28 @@ static cudaError_t gemv_dispatch_em(const GemvArgs& a, int XM, int EM, int grid,
     return cudaErrorInvalidValue;
 }
 
+cudaError_t SKB_CAT(gemv_launch_m, GEMV_M)(const GemvArgs& a, int KQ, int XM, int EM, const RgPlan& p,
+                                           cudaStream_t s, bool pdl) {
+    switch (KQ) {
+        case 8: return gemv_dispatch_em<8>(a, XM, EM, p, s, pdl);
+        case 16: return gemv_dispatch_em<16>(a, XM, EM, p, s, pdl);
+        case 24: return gemv_dispatch_em<24>(a, XM, EM, p, s, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t SKB_CAT(gemv_prepare_m, GEMV_M)() {
     GemvArgs a = {};
+    RgPlan p;  // grid 0: set attributes only
     const int pairs[9][2] = {{X_PLAIN, E_STORE}, {X_PLAIN, E_RESID}, {X_PLAIN, E_BIAS}, {X_PLAIN, E_SWIGLU},
                              {X_RMSNORM, E_STORE}, {X_RMSNORM, E_SWIGLU}, {X_RMSNORM, E_BIAS},
                              {X_ADD_RMSNORM, E_SWIGLU}, {X_NORM_ADD_NORM, E_SWIGLU}};
-    for (int kv4 = 1; kv4 <= 4; ++kv4)
-        for (auto& p : pairs) {
-            cudaError_t e = SKB_CAT(gemv_launch_m, GEMV_M)(a, kv4, p[0], p[1], 0, nullptr, false);
+    for (int kq : {8, 16, 24})
+        for (auto& pr : pairs) {
+            cudaError_t e = SKB_CAT(gemv_launch_m, GEMV_M)(a, kq, pr[0], pr[1], p, nullptr, false);
             if (e != cudaSuccess) return e;
         }
     return cudaSuccess;
-}
-
-cudaError_t SKB_CAT(gemv_launch_m, GEMV_M)(const GemvArgs& a, int KV4, int XM, int EM, int grid,
-                                           cudaStream_t s, bool pdl) {
-    switch (KV4) {
-        case 1: return gemv_dispatch_em<1>(a, XM, EM, grid, s, pdl);
-        case 2: return gemv_dispatch_em<2>(a, XM, EM, grid, s, pdl);
-        case 3: return gemv_dispatch_em<3>(a, XM, EM, grid, s, pdl);
-        case 4: return gemv_dispatch_em<4>(a, XM, EM, grid, s, pdl);
-        default: return cudaErrorInvalidValue;
-    }
 }
 
 }  // namespace skb

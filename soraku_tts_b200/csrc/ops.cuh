@@ -17,9 +17,10 @@ int cfg_sample(const float* logits, int rows_per_req, int n_req, int V,
                float* uniforms, cudaStream_t s, bool pdl);
 GemvArgs gemv_args_plain(const float* x, int ldx, int N, int K);
 
-cudaError_t gemv_launch_m1(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
-cudaError_t gemv_launch_m2(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
-cudaError_t gemv_launch_m4(const GemvArgs& a, int KV4, int XM, int EM, int grid, cudaStream_t s, bool pdl);
+struct RgPlan;
+cudaError_t gemv_launch_m1(const GemvArgs& a, int KQ, int XM, int EM, const RgPlan& p, cudaStream_t s, bool pdl);
+cudaError_t gemv_launch_m2(const GemvArgs& a, int KQ, int XM, int EM, const RgPlan& p, cudaStream_t s, bool pdl);
+cudaError_t gemv_launch_m4(const GemvArgs& a, int KQ, int XM, int EM, const RgPlan& p, cudaStream_t s, bool pdl);
 cudaError_t gemv_prepare_m1();
 cudaError_t gemv_prepare_m2();
 cudaError_t gemv_prepare_m4();

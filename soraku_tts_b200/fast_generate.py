@@ -29,8 +29,7 @@ from .model import as_soraku_model
 class FastGenerator:
     def __init__(self, model, *, device: torch.device, use_tilelang: bool = True, compile_trunk: bool = False,
                  batch_branches: bool = True, native_sampling: bool = True, use_graph: bool = True,
-                 frames_per_graph: int = 8, use_pdl: bool = True, l2_prefetch: bool = True,
-                 persistent: bool = False):
+                 frames_per_graph: int = 8, use_pdl: bool = True, l2_prefetch: bool = True):
         self.model = as_soraku_model(model, device)
         self.config = self.model.config
         self.device = torch.device(device)
@@ -39,7 +38,6 @@ class FastGenerator:
         self.frames_per_graph = int(frames_per_graph)
         self.use_pdl = use_pdl
         self.l2_prefetch = l2_prefetch
-        self.persistent = persistent
         self._engine: NativeEngine | None = None
         self._graph_key = None
         self.last_timing: dict[str, float] = {}
@@ -52,7 +50,7 @@ class FastGenerator:
             self._engine = NativeEngine(self.model, max_requests=1, rows_per_request=rows,
                                         max_len=max(max_len, 512), max_frames=max(max_frames, 512),
                                         max_prefill=max(max_len, 512), use_pdl=self.use_pdl,
-                                        l2_prefetch=self.l2_prefetch, persistent=self.persistent)
+                                        l2_prefetch=self.l2_prefetch)
             self._graph_key = None
         return self._engine
 

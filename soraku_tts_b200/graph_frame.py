@@ -16,9 +16,7 @@ Differences from the reference, all semantics-preserving:
   ``torch.multinomial``; greedy decoding (``sampled=False``) is argmax as in
   the reference;
 * ``top_k``/``top_p`` are runtime parameters, so changing them needs no
-  recapture;
-* ``persistent=True`` records each frame chunk as one persistent cooperative
-  kernel instead of the separate-kernel sequence.
+  recapture.
 """
 
 from __future__ import annotations
@@ -42,12 +40,11 @@ class NativeEngine:
     """Thin owner of an ``skb_engine*`` (the C ABI of include/soraku_b200.h)."""
 
     def __init__(self, model, *, max_requests=1, rows_per_request=2, max_len=1024, max_frames=1024,
-                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True,
-                 persistent=False):
+                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True):
         self.model = model
         opts = _lib.skb_engine_opts(max_requests, rows_per_request, max_len, max_frames,
                                     max_prefill if max_prefill else max_len, page_size, attn_splits,
-                                    1 if use_pdl else 0, 1 if l2_prefetch else 0, 1 if persistent else 0)
+                                    1 if use_pdl else 0, 1 if l2_prefetch else 0)
         handle = ctypes.c_void_p()
         desc = model.model_desc()
         _lib.call("skb_engine_create", ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
@@ -131,9 +128,6 @@ class NativeEngine:
         """Kernel launches of one step() of the captured graph."""
         return int(_lib.lib().skb_engine_launches_per_step(self.h))
 
-    def is_persistent(self) -> bool:
-        return bool(_lib.lib().skb_engine_is_persistent(self.h))
-
 
 def _host_ids(ids) -> torch.Tensor:
     t = torch.as_tensor(ids).to("cpu", torch.int64).reshape(-1).contiguous()
@@ -157,7 +151,7 @@ class GraphFrameEngine:
 
     def __init__(self, model, *, device: torch.device, max_cache_len: int, cfg_scale: float = 1.5,
                  batch: int = 2, max_frames: int | None = None, use_pdl: bool = True,
-                 l2_prefetch: bool = True, persistent: bool = False) -> None:
+                 l2_prefetch: bool = True) -> None:
         if batch not in (1, 2):
             raise ValueError("batch must be 1 (no CFG) or 2 (cond + uncond)")
         self.model = as_soraku_model(model, device)
@@ -170,7 +164,7 @@ class GraphFrameEngine:
         self.max_len = int(max_cache_len)
         self.native = NativeEngine(self.model, max_requests=1, rows_per_request=batch, max_len=self.max_len,
                                    max_frames=max_frames or self.max_len, max_prefill=self.max_len,
-                                   use_pdl=use_pdl, l2_prefetch=l2_prefetch, persistent=persistent)
+                                   use_pdl=use_pdl, l2_prefetch=l2_prefetch)
         self.cfg = torch.tensor([cfg_scale], device=self.device, dtype=torch.float32)
         self.graph = None
         self.top_k: int | None = None
