@@ -1,0 +1,352 @@
+// Decode attention, one thread-block cluster per (row, kv head).
+//
+// Grid (C, KVH, R) with cluster dims (C, 1, 1), C <= 8.  CTA s of the cluster
+// owns positions [s*T/C, (s+1)*T/C) of the row's T = p_new + 1 positions.
+//
+// Before the programmatic-dependent-launch wait -- everything it reads was
+// written by kernels at least two launches back (the cache positions before
+// p_new by earlier frames, the row position by the previous frame's last
+// kernel) -- thread 0 looks up the pages of its range and stages the cached
+// K and V rows into shared memory with 1-D bulk copies (TMA engine, one copy
+// per page run, no multicast); the RoPE row of p_new and the q/k norm weights
+// go to registers.  After the wait only the new q, k, v rows are read (one
+// round trip).  Scores, softmax and P.V run on shared memory; the C partial
+// (max, sum, output) triples are merged in split order by the cluster's rank
+// 0 through distributed shared memory, so no global partials, atomics or
+// second launch are needed.  Ranges longer than ATC_PMAX positions are
+// processed in rounds with an online softmax.
+//
+// (The merge area, ATC_MAXC partials, lives in rank 0's K buffer.)
+//
+// Arithmetic restates transformers' Qwen3 attention step (modeling_qwen3.py:
+// q_norm/k_norm :248-249, RoPE :130-181, GQA softmax :184-219, scaling
+// head_dim**-0.5 :232).
+#include "ops.cuh"
+#include "trunk.cuh"
+#include "trunk_api.cuh"
+
+namespace skb {
+
+constexpr int ATC_THREADS = 256;
+constexpr int ATC_PMAX = 112;  // cached positions staged per round
+constexpr int ATC_MAXC = 8;    // CTAs per cluster (portable cluster size)
+constexpr int ATC_PART = 260;  // floats of one pushed partial: o[2][128], m[2], l[2]
+
+struct AtcSmem {
+    float k[ATC_PMAX][128];
+    float v[ATC_PMAX][128];
+    float q[2][128];
+    float kn[128];
+    float vn[128];
+    float p[2][ATC_PMAX + 4];  // scores, then probabilities (+ the new position)
+    float mr[2], lr[2];        // per-round block max / sum
+    uint64_t bar;
+    int err;
+};
+static_assert(ATC_MAXC * ATC_PART <= ATC_PMAX * 128, "merge area must fit in the K buffer");
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store of a float into the shared memory of CTA `rank` of this cluster.
+__device__ __forceinline__ void st_dsmem(float* p, float v, uint32_t rank) {
+    uint32_t a = smem_u32(p), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+// Issues the bulk copies of cached positions [p0, p1) of (row r, head g)
+// into sm.k / sm.v (index = position - p0); returns the bytes requested.
+__device__ uint32_t atc_stage(const DecodeAttnArgs& a, int r, int g, int p0, int p1, AtcSmem& sm) {
+    uint32_t bytes = 0;
+    const int page_sz = 1 << a.kv.page_log2;
+    int p = p0;
+    while (p < p1) {
+        const int end = min(p1, ((p >> a.kv.page_log2) + 1) * page_sz);
+        bytes += (uint32_t)(end - p) * 1024u;
+        p = end;
+    }
+    if (bytes == 0) return 0;
+    mbar_expect_tx(&sm.bar, bytes);
+    p = p0;
+    while (p < p1) {
+        const int end = min(p1, ((p >> a.kv.page_log2) + 1) * page_sz);
+        int page = __ldcg(a.kv.page_table + r * a.kv.max_pages + (p >> a.kv.page_log2));
+        if ((unsigned)page >= (unsigned)a.kv.n_pages) page = 0;
+        const int slot = p & (page_sz - 1);
+        const float* kb = a.kv.pool + a.layer * a.kv.layer_floats +
+                          ((((long long)page * 2 + 0) * a.kv.KVH + g) << a.kv.page_log2) * 128 + (long long)slot * 128;
+        const float* vb = kb + ((long long)a.kv.KVH << a.kv.page_log2) * 128;
+        const uint32_t nb = (uint32_t)(end - p) * 512u;
+        bulk_g2s(&sm.k[p - p0][0], kb, nb, &sm.bar);
+        bulk_g2s(&sm.v[p - p0][0], vb, nb, &sm.bar);
+        p = end;
+    }
+    return bytes;
+}
+
+__global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const DecodeAttnArgs a) {
+    extern __shared__ __align__(128) unsigned char atc_raw[];
+    AtcSmem& sm = *reinterpret_cast<AtcSmem*>(atc_raw);
+    const int s = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+    const int C = gridDim.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n_rep = a.n_rep;
+
+    if (tid == 0) {
+        stamp_min(a.ts);
+        mbar_init(&sm.bar, 1);
+        mbar_fence_init();
+        sm.err = 0;
+    }
+    __syncthreads();
+
+    // ---- before the wait: position, pages, cached K/V, RoPE row, norm weights
+    int p_new = __ldcg(a.pos + r);
+    const bool bad_pos = p_new < 0 || p_new >= a.max_len;
+    if (bad_pos) p_new = p_new < 0 ? 0 : a.max_len - 1;
+    const int T = p_new + 1;
+    const int pb = (int)((long long)s * T / C);
+    const int pe = (int)((long long)(s + 1) * T / C);
+    const bool own_new = pe == T;            // the last CTA holds position p_new
+    const int cend = own_new ? p_new : pe;   // cached positions [pb, cend)
+    const int n_cached = cend > pb ? cend - pb : 0;
+    const int n_rounds = n_cached > 0 ? (n_cached + ATC_PMAX - 1) / ATC_PMAX : 1;
+    if (tid == 0) {
+        atc_stage(a, r, g, pb, pb + min(n_cached, ATC_PMAX), sm);
+        // later rounds (long contexts): into L2 now, into shared memory later
+        for (int p = pb + ATC_PMAX; p < cend;) {
+            const int end = min(cend, ((p >> a.kv.page_log2) + 1) << a.kv.page_log2);
+            const float* kb = a.kv.at(a.layer, r, p, 0, g);
+            const float* vb = a.kv.at(a.layer, r, p, 1, g);
+            bulk_prefetch_l2(kb, (unsigned)(end - p) * 512u);
+            bulk_prefetch_l2(vb, (unsigned)(end - p) * 512u);
+            p = end;
+        }
+    }
+    const float* cosr = a.rope_cos + (size_t)p_new * 64;
+    const float* sinr = a.rope_sin + (size_t)p_new * 64;
+    // cache slots of p_new (the page lookup is done before the wait too)
+    float* kdst = (own_new && warp == 2) ? a.kv.at(a.layer, r, p_new, 0, g) : nullptr;
+    float* vdst = (own_new && warp == 3) ? a.kv.at(a.layer, r, p_new, 1, g) : nullptr;
+
+    pdl_wait();
+    if (tid == 0) stamp_wait(a.ts);
+    if (tid == 0 && bad_pos && a.err != nullptr) atomicExch(a.err, 1);
+
+    // ---- the new q (n_rep heads), k and v of this kv head: one round trip
+    const float* row = a.qkv + (size_t)r * a.ld_qkv;
+    if (warp < n_rep) {
+        const int h = g * n_rep + warp;
+        float4 q = ld_cg4(reinterpret_cast<const float4*>(row + h * 128) + lane);
+        q = norm_rope_head(q, a.qn, a.eps, cosr, sinr, lane, true, true);
+        q.x *= a.scale;
+        q.y *= a.scale;
+        q.z *= a.scale;
+        q.w *= a.scale;
+        reinterpret_cast<float4*>(sm.q[warp])[lane] = q;
+    } else if (warp == 2) {
+        float4 k = ld_cg4(reinterpret_cast<const float4*>(row + (a.H + g) * 128) + lane);
+        k = norm_rope_head(k, a.kn, a.eps, cosr, sinr, lane, true, true);
+        reinterpret_cast<float4*>(sm.kn)[lane] = k;
+        if (kdst) reinterpret_cast<float4*>(kdst)[lane] = k;
+    } else if (warp == 3) {
+        const float4 v = ld_cg4(reinterpret_cast<const float4*>(row + (a.H + a.kv.KVH + g) * 128) + lane);
+        reinterpret_cast<float4*>(sm.vn)[lane] = v;
+        if (vdst) reinterpret_cast<float4*>(vdst)[lane] = v;
+    }
+    pdl_trigger();
+    __syncthreads();
+
+    // ---- rounds of up to ATC_PMAX cached positions (+ p_new in the last)
+    const int hh = tid >> 7, d = tid & 127;  // P.V: thread (head hh, dim d)
+    float o_run = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    uint32_t phase = 0;
+    for (int rd = 0; rd < n_rounds; ++rd) {
+        // a copy that timed out stops the rounds (sm.err was written before
+        // the last barrier, so every thread takes the same branch)
+        if (sm.err) break;
+        const int r0 = pb + rd * ATC_PMAX;
+        const int nc = max(0, min(ATC_PMAX, cend - r0));  // cached positions this round
+        const bool last = rd == n_rounds - 1;
+        const int ns = nc + ((last && own_new) ? 1 : 0);  // score slots
+        if (rd > 0 && tid == 0) atc_stage(a, r, g, r0, r0 + nc, sm);
+        if (nc > 0) {
+            if (!mbar_wait(&sm.bar, phase, a.err)) sm.err = 1;
+            phase ^= 1u;
+        }
+        // scores: warp w takes slots w*4 .. w*4+3, then +32; 4 slots x 2 heads
+        // per butterfly (lane group l>>2 ends with value (slot l>>3, head (l>>2)&1))
+        const float4 q0 = reinterpret_cast<const float4*>(sm.q[0])[lane];
+        const float4 q1 = reinterpret_cast<const float4*>(sm.q[n_rep > 1 ? 1 : 0])[lane];
+        for (int i0 = warp * 4; i0 < ns; i0 += 32) {
+            float vals[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = i0 + j;
+                float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i < nc) kv = reinterpret_cast<const float4*>(sm.k[i])[lane];
+                else if (i < ns) kv = reinterpret_cast<const float4*>(sm.kn)[lane];
+                vals[2 * j] = q0.x * kv.x + q0.y * kv.y + q0.z * kv.z + q0.w * kv.w;
+                vals[2 * j + 1] = q1.x * kv.x + q1.y * kv.y + q1.z * kv.z + q1.w * kv.w;
+            }
+            const float res = butterfly_reduce<8>(vals, lane);
+            if ((lane & 3) == 0) {
+                const int vi = lane >> 2, i = i0 + (vi >> 1), h = vi & 1;
+                if (i < ns && h < n_rep) sm.p[h][i] = res;
+            }
+        }
+        __syncthreads();
+        // per-head max (warp h), then probabilities and their sum (warp h)
+        if (warp < n_rep) {
+            float mx = -INFINITY;
+            for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, sm.p[warp][i]);
+            mx = warp_max(mx);
+            const float mnew = fmaxf(m_run[warp], mx);
+            float sum = 0.f;
+            for (int i = lane; i < ns; i += 32) {
+                const float e = (mnew == -INFINITY) ? 0.f : expf(sm.p[warp][i] - mnew);
+                sm.p[warp][i] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                sm.mr[warp] = mnew;
+                sm.lr[warp] = sum;
+            }
+        }
+        __syncthreads();
+        // online update of (m, l, o) and P.V over this round's slots
+        float mnew[2], corr[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            mnew[h] = h < n_rep ? sm.mr[h] : -INFINITY;
+            corr[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew[h]);
+            l_run[h] = l_run[h] * corr[h] + (h < n_rep ? sm.lr[h] : 0.f);
+            m_run[h] = mnew[h];
+        }
+        if (hh < n_rep) {
+            float acc = o_run * corr[hh];
+            const float* pr = sm.p[hh];
+            int i = 0;
+            for (; i + 4 <= nc; i += 4) {
+                acc = fmaf(pr[i], sm.v[i][d], acc);
+                acc = fmaf(pr[i + 1], sm.v[i + 1][d], acc);
+                acc = fmaf(pr[i + 2], sm.v[i + 2][d], acc);
+                acc = fmaf(pr[i + 3], sm.v[i + 3][d], acc);
+            }
+            for (; i < nc; ++i) acc = fmaf(pr[i], sm.v[i][d], acc);
+            if (ns > nc) acc = fmaf(pr[nc], sm.vn[d], acc);
+            o_run = acc;
+        }
+        __syncthreads();  // sm.k / sm.v / sm.p are refilled by the next round
+    }
+
+    // ---- merge: once every CTA of the cluster is done with its K/V buffers,
+    // each pushes its partial (max, sum, output) into rank 0's K buffer with
+    // remote stores; after a second cluster barrier rank 0 merges them in
+    // split order from its own shared memory.
+    if (tid == 0 && sm.err) {
+        // a copy did not arrive in time: flag it and wait (bounded) once more
+        // so that no copy is still in flight when the buffers are reused
+        if (a.err != nullptr) atomicExch(a.err, 1);
+        mbar_wait(&sm.bar, phase ^ 1u, nullptr);
+    }
+    cluster_sync_all();
+    const uint32_t rank = cluster_ctarank();
+    float* slot = &sm.k[0][0] + (size_t)rank * ATC_PART;  // [2][128] o | [2] m | [2] l
+    if (hh < n_rep) {
+        st_dsmem(slot + hh * 128 + d, o_run, 0);
+        if (d == 0) {
+            st_dsmem(slot + 256 + hh, m_run[hh], 0);
+            st_dsmem(slot + 258 + hh, l_run[hh], 0);
+        }
+    }
+    cluster_sync_all();
+    if (rank == 0 && hh < n_rep) {
+        const float* parts = &sm.k[0][0];
+        float M = -INFINITY;
+        for (int j = 0; j < C; ++j) M = fmaxf(M, parts[j * ATC_PART + 256 + hh]);
+        float L = 0.f, O = 0.f;
+        for (int j = 0; j < C; ++j) {
+            const float* pj = parts + j * ATC_PART;
+            const float mj = pj[256 + hh];
+            const float w = (mj == -INFINITY) ? 0.f : expf(mj - M);
+            L = fmaf(pj[258 + hh], w, L);
+            O = fmaf(pj[hh * 128 + d], w, O);
+        }
+        a.out[(size_t)r * a.H * 128 + (g * n_rep + hh) * 128 + d] = O / L;
+    }
+    if (a.ts) {
+        __syncthreads();
+        if (tid == 0) stamp_max(a.ts + 3);
+    }
+}
+
+cudaError_t decode_attn_cluster_prepare() {
+    return set_smem_attrs(decode_attn_cluster_kernel, sizeof(AtcSmem));
+}
+
+// Widest cluster (<= 8 CTAs) for which `groups` clusters can be resident at
+// once on this GPU (a cluster's CTAs must share one GPC; with ~119 KB of shared
+// memory per CTA a B200 holds 15 clusters of 8 but needs 16 at bs1 CFG).
+int decode_attn_cluster_width(int groups) {
+    if (decode_attn_cluster_prepare() != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+    }
+    for (int c = ATC_MAXC; c > 1; --c) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c, 1, 1);
+        cfg.blockDim = dim3(ATC_THREADS);
+        cfg.dynamicSmemBytes = sizeof(AtcSmem);
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = c;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, decode_attn_cluster_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        if (n >= groups) return c;
+    }
+    return 1;
+}
+
+// C = a.S CTAs per (row, kv head), 1 <= C <= 8; head_dim 128, n_rep <= 2.
+cudaError_t decode_attn_cluster_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl) {
+    static bool prepared = false;
+    if (!prepared) {
+        const cudaError_t e = decode_attn_cluster_prepare();
+        if (e != cudaSuccess) return e;
+        prepared = true;
+    }
+    if (a.S < 1 || a.S > ATC_MAXC || a.n_rep < 1 || a.n_rep > 2 || a.kv.hd != 128) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.S, a.kv.KVH, R);
+    cfg.blockDim = dim3(ATC_THREADS);
+    cfg.dynamicSmemBytes = sizeof(AtcSmem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel, a);
+}
+
+}  // namespace skb

@@ -189,7 +189,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
 }
 
+// --------------------------------------------------------- kernel stamps
+// Debug timeline of one launch (all null unless the engine's debug mode is
+// on): ts[0] earliest CTA start, ts[1] earliest and ts[2] latest release from
+// the programmatic-dependent-launch wait, ts[3] latest CTA end (%globaltimer ns).
+__device__ __forceinline__ void stamp_min(unsigned long long* p) {
+    if (p) atomicMin(p, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void stamp_max(unsigned long long* p) {
+    if (p) atomicMax(p, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void stamp_wait(unsigned long long* ts) {
+    if (ts) {
+        const unsigned long long t = globaltimer_ns();
+        atomicMin(ts + 1, t);
+        atomicMax(ts + 2, t);
+    }
+}
+
 // --------------------------------------------------------------- launching
+// Dynamic shared-memory limit plus the largest shared-memory carveout.  Every
+// decode kernel asks for the same carveout: an SM can only hold CTAs of
+// kernels whose carveouts agree, and a programmatic dependent launch is only
+// useful when the next kernel's CTAs can join the running ones.
+template <typename K>
+inline cudaError_t set_smem_attrs(K* kernel, size_t dyn_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+    return e;
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                           cudaStream_t stream, bool pdl, Args&&... args) {

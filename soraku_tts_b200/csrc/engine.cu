@@ -37,10 +37,16 @@ namespace skb {
 __global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const DepthSampleArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int codes_s[32];
+    if (threadIdx.x == 0) stamp_min(a.ts);
     prefetch_share(a.pf, blockIdx.x, gridDim.x);
     pdl_wait();
+    if (threadIdx.x == 0) stamp_wait(a.ts);
     pdl_trigger();
     depth_sample_body<BlockSync, SAMPLER_VMAX>(a, blockIdx.x, smem, codes_s);
+    if (a.ts) {
+        __syncthreads();
+        if (threadIdx.x == 0) stamp_max(a.ts + 3);
+    }
 }
 
 }  // namespace skb
@@ -54,13 +60,13 @@ struct skb_engine {
     int device = 0, nsm = 148;
     int R = 0, rpr = 1, nreq = 0;
     int D = 0, H = 0, KVH = 0, hd = 0, F = 0, I = 0, Q = 0, V = 0, L = 0, n_rep = 1;
-    int max_pages = 0, page_log2 = 6, S = 1, nmax = 1;
+    int max_pages = 0, page_log2 = 6, S = 1;
     long long layer_floats = 0;
     // decode state
     float *x = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *abuf = nullptr, *y = nullptr,
-          *hidden = nullptr, *logits = nullptr, *logits_hist = nullptr, *prefix = nullptr, *part = nullptr,
+          *hidden = nullptr, *logits = nullptr, *logits_hist = nullptr, *prefix = nullptr,
           *rope_cos = nullptr, *rope_sin = nullptr, *kv = nullptr;
-    int *pos = nullptr, *counters = nullptr, *page_table = nullptr, *err = nullptr, *host_flag = nullptr;
+    int *pos = nullptr, *page_table = nullptr, *err = nullptr, *host_flag = nullptr;
     int64_t *cur_codes = nullptr, *hist = nullptr;
     ReqState* st = nullptr;
     // prefill scratch
@@ -74,6 +80,7 @@ struct skb_engine {
     cudaGraphExec_t exec = nullptr;
     int graph_active = 0, graph_fpg = 0, graph_pdl = 0;
     int debug = 0;
+    unsigned long long* kts = nullptr;  // debug kernel timeline [kernels per frame][4]
     std::vector<int> frames_host, pos_host;
     std::vector<ReqState> st_host;
     std::vector<void*> allocs;
@@ -280,10 +287,7 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
             a.H = e->H;
             a.n_rep = e->n_rep;
             a.S = e->S;
-            a.nmax = e->nmax;
             a.scale = 1.0f / sqrtf((float)e->hd);
-            a.part = e->part;
-            a.counters = e->counters;
             a.out = e->attn;
             a.err = e->err;
             Phase ph = {};
@@ -333,11 +337,15 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
 std::vector<Node> build_frame(skb_engine* e, int n_active) {
     const int R = n_active * e->rpr;
     std::vector<Node> nodes;
+    auto stamps = [e, &nodes]() { return e->debug ? e->kts + 4 * nodes.size() : nullptr; };
     for (const Phase& ph : build_phases(e, n_active)) {
         if (ph.kind == PH_GEMV) {
-            nodes.push_back(gemv_node(e, ph.g, R, ph.xm, ph.em));
+            GemvArgs g = ph.g;
+            g.ts = stamps();
+            nodes.push_back(gemv_node(e, g, R, ph.xm, ph.em));
             if (ph.sample) {
-                const DepthSampleArgs a = ph.s;
+                DepthSampleArgs a = ph.s;
+                a.ts = stamps();
                 Node n;
                 n.ctas = n_active;
                 n.run = [a, n_active](cudaStream_t s, bool pdl, const PrefetchList& pf) {
@@ -348,13 +356,14 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
                 nodes.push_back(n);
             }
         } else {
-            const DecodeAttnArgs a = ph.at;
+            DecodeAttnArgs a = ph.at;
+            a.ts = stamps();
             Node n;
             n.ctas = a.S * e->KVH * R;
             n.run = [a, R](cudaStream_t s, bool pdl, const PrefetchList& pf) {
                 DecodeAttnArgs b = a;
                 b.pf = pf;
-                return decode_attn_launch(b, R, s, pdl);
+                return decode_attn_cluster_launch(b, R, s, pdl);
             };
             nodes.push_back(n);
         }
@@ -478,10 +487,10 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     while ((1 << e->page_log2) < ps) ++e->page_log2;
     e->o.page_size = 1 << e->page_log2;
     e->max_pages = (opts->max_len + e->o.page_size - 1) / e->o.page_size;
-    // one (row, kv head, split) item per SM
-    e->S = opts->attn_splits > 0 ? opts->attn_splits : (e->nsm / (e->R * e->KVH) > 0 ? e->nsm / (e->R * e->KVH) : 1);
-    if (e->S > 512) e->S = 512;  // the split combine stages S x 2 (max, sum) pairs in 8 KB of shared memory
-    e->nmax = (opts->max_len + e->S - 1) / e->S + 1;
+    // CTAs per (row, kv head): one cluster, as wide as lets every (row, kv
+    // head) cluster be resident at once
+    e->S = opts->attn_splits > 0 ? opts->attn_splits : decode_attn_cluster_width(e->R * e->KVH);
+    if (e->S > 8) e->S = 8;
     const size_t n_pages = (size_t)e->R * e->max_pages;
     e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;
     const int qkvd = (e->H + 2 * e->KVH) * e->hd;
@@ -500,14 +509,13 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->logits, (size_t)e->R * e->V)
     A(e->logits_hist, (size_t)e->Q * e->R * e->V)
     A(e->prefix, (size_t)e->nreq * e->D)
-    A(e->part, (size_t)e->R * e->KVH * e->S * e->n_rep * (e->hd + 2))
     A(e->rope_cos, (size_t)opts->max_len * (e->hd / 2))
     A(e->rope_sin, (size_t)opts->max_len * (e->hd / 2))
     A(e->kv, (size_t)e->L * e->layer_floats)
     A(e->pos, e->R)
-    A(e->counters, (size_t)e->R * e->KVH)
     A(e->page_table, (size_t)e->R * e->max_pages)
     A(e->err, 8)
+    A(e->kts, (size_t)4 * (e->Q * 4 + e->L * 5))
     A(e->host_flag, 1)
     A(e->cur_codes, (size_t)e->nreq * e->Q)
     A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
@@ -562,7 +570,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
         skb_engine_destroy(e);
         return fail(SKB_ERR_CUDA, "stream creation failed");
     }
-    cudaFuncSetAttribute(depth_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SAMPLER_SMEM);
+    set_smem_attrs(depth_sample_kernel, SAMPLER_SMEM);
+    decode_attn_cluster_prepare();
     trunk_init_attrs();
     gemv_prepare_all();
     const cudaError_t ce = cudaDeviceSynchronize();
@@ -878,6 +887,7 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
         case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
+        case 8: *ptr = e->kts; *numel = (int64_t)4 * skb_engine_kernels_per_frame(e); break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }
     return SKB_OK;

@@ -29,6 +29,7 @@ struct DepthSampleArgs {
     int max_frames;
     int bos, pad, eos;
     PrefetchList pf;
+    unsigned long long* ts;  // optional debug timeline [4]
 };
 
 // One request's sampling step for codebook a.q and its epilogue: the code goes

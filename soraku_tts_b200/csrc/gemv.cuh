@@ -68,6 +68,7 @@ struct GemvArgs {
     int n_inc;
     int* err;   // optional: set to 1 if a weight copy did not arrive
     PrefetchList pf;
+    unsigned long long* ts;  // optional debug timeline [4] (see stamp_wait)
 };
 
 __device__ __forceinline__ const float* gemv_row(const GemvArgs& a, int r) {

@@ -176,8 +176,7 @@ int cfg_sample(const float* logits, int rows_per_req, int n_req, int V,
                float* uniforms, cudaStream_t s, bool pdl) {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(cfg_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SAMPLER_SMEM);
+        set_smem_attrs(cfg_sample_kernel, SAMPLER_SMEM);
         attr_set = true;
     }
     cudaError_t e = launch(cfg_sample_kernel, dim3(n_req), dim3(SAMPLER_THREADS), SAMPLER_SMEM, s,

@@ -110,6 +110,7 @@ __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots)
     const int K4 = a.K >> 2;
 
     if (threadIdx.x == 0) {
+        stamp_min(a.ts);
         for (int s = 0; s < S; ++s) {
             mbar_init(&hd.full[s], 1);
             mbar_init(&hd.empty[s], RG_CWARPS);
@@ -163,6 +164,7 @@ __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots)
         for (int t = tid; t < nunits; t += 32 * RG_CWARPS) epi[t] = __ldg(a.bias + u0 + t);
 
     pdl_wait();
+    if (tid == 0) stamp_wait(a.ts);
     if (a.inc != nullptr && blockIdx.x == 0 && tid < a.n_inc) atomicAdd(a.inc + tid, 1);
 
     float4 xo[M][QW], x2o[ADD ? M : 1][QW];
@@ -339,6 +341,10 @@ __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&hd.empty[s]);
+    }
+    if (a.ts) {
+        named_sync_consumers();
+        if (tid == 0) stamp_max(a.ts + 3);
     }
     if (!ok && lane == 0) {
         // a copy never arrived: let the producer stop, then wait (bounded) for

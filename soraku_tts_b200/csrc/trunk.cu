@@ -12,10 +12,16 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const DecodeAttnArgs a
     __shared__ AttnSmem sm;
     const int s = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
     const int nblk = gridDim.x * gridDim.y * gridDim.z;
+    if (threadIdx.x == 0) stamp_min(a.ts);
     prefetch_share(a.pf, (r * gridDim.y + g) * gridDim.x + s, nblk);
     pdl_wait();
+    if (threadIdx.x == 0) stamp_wait(a.ts);
     pdl_trigger();
     decode_attn_item<BlockSync>(a, s, g, r, sm);
+    if (a.ts) {
+        __syncthreads();
+        if (threadIdx.x == 0) stamp_max(a.ts + 3);
+    }
 }
 
 cudaError_t decode_attn_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl) {
@@ -356,7 +362,8 @@ cudaError_t prefill_attn_launch(const float* Q, const int* row_off, const int* r
 }
 
 cudaError_t trunk_init_attrs() {
-    return cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PATTN_SMEM);
+    const cudaError_t e = set_smem_attrs(decode_attn_kernel, 0);
+    return e != cudaSuccess ? e : set_smem_attrs(prefill_attn_kernel, PATTN_SMEM);
 }
 
 cudaError_t gather_rows_launch(const float* X, const int* src, const int* dst, int n, float* out,
@@ -406,7 +413,11 @@ int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, cons
     a.out = out;
     a.err = nullptr;
     a.kv.n_pages = n_pages;
-    cudaError_t e = decode_attn_launch(a, rows, stream, false);
+    // up to 8 splits: one thread-block cluster per (row, kv head), merged in
+    // distributed shared memory (the scratch is not touched); more splits:
+    // partials in the caller's scratch, merged by the last CTA
+    cudaError_t e = splits <= 8 ? decode_attn_cluster_launch(a, rows, stream, false)
+                                : decode_attn_launch(a, rows, stream, false);
     return e == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
 }
 

@@ -47,6 +47,7 @@ struct DecodeAttnArgs {
     float* out;     // [R][H*hd]
     int* err;
     PrefetchList pf;
+    unsigned long long* ts;  // optional debug timeline [4]
 };
 
 // prefill

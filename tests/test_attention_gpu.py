@@ -69,7 +69,7 @@ def run(c, splits):
 
 
 @pytest.mark.parametrize("lengths", [[37, 300], [0, 5], [511, 63]])
-@pytest.mark.parametrize("splits", [1, 9, 40])
+@pytest.mark.parametrize("splits", [1, 3, 8, 9, 40])
 def test_decode_attention_matches_oracle(lengths, splits):
     c = make_case(lengths, seed=sum(lengths) + splits)
     got, pool = run(c, splits)
