@@ -255,10 +255,11 @@ int skb_engine_frames(skb_engine *eng, int request);
  * [R, d]; 1 hidden [R, d]; 2 logits [R, V] of the last depth step; 3 pos
  * int32 [R]; 4 logits history [Q, R, V] of the last frame (debug capture must
  * be on); 5 prefix [n_req, d]; 6 error flags int32 [8]; 7 request state;
- * 8 kernel timeline uint64 [kernels per frame][4] of the last replayed frame
- * with debug on: earliest CTA start, earliest and latest release from the
- * dependent-launch wait, latest CTA end (%globaltimer ns; the caller resets
- * it to {max, max, 0, 0} before the frame). */
+ * 8 kernel timeline uint64 [kernels per frame][16] of the last replayed
+ * frame with debug on: earliest CTA start, earliest and latest release from
+ * the dependent-launch wait, latest CTA end, then the latest CTA to reach
+ * kernel-specific points (%globaltimer ns; the caller resets it to
+ * {max, max, 0, ...} before the frame). */
 int skb_engine_view(skb_engine *eng, int which, void **ptr, int64_t *numel);
 
 /* Keep the per-(q) logits of the last frame in the history buffer (view 4). */

@@ -41,6 +41,7 @@ struct AtcSmem {
     float p[2][ATC_PMAX + 4];  // scores, then probabilities (+ the new position)
     float mr[2], lr[2];        // per-round block max / sum
     uint64_t bar;
+    uint64_t merge_bar;  // rank 0: every CTA's partial has arrived
     int err;
 };
 static_assert(ATC_MAXC * ATC_PART <= ATC_PMAX * 128, "merge area must fit in the K buffer");
@@ -50,14 +51,22 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+// Cluster barrier whose arrive orders no memory (relaxed) and whose wait
+// acquires: the CTAs learn that every CTA finished reading its own shared
+// memory, and see mbarriers initialised before a fence.mbarrier_init.
+__device__ __forceinline__ void cluster_sync_exec() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Store of a float into the shared memory of CTA `rank` of this cluster.
-__device__ __forceinline__ void st_dsmem(float* p, float v, uint32_t rank) {
-    uint32_t a = smem_u32(p), ra;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+// Asynchronous store of a float into the shared memory of CTA `rank` of this
+// cluster, completing (4 bytes of transaction count) on that CTA's mbarrier
+// at the same offset as `bar`.
+__device__ __forceinline__ void st_async_f32(float* p, float v, uint64_t* bar, uint32_t rank) {
+    uint32_t rp, rb;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rp) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(smem_u32(bar)), "r"(rank));
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(rp),
+                 "r"(__float_as_uint(v)), "r"(rb)
+                 : "memory");
 }
 
 // Issues the bulk copies of cached positions [p0, p1) of (row r, head g)
@@ -98,10 +107,16 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n_rep = a.n_rep;
 
+    // debug stage times of this thread, flushed at the end so that no global
+    // atomic sits before a barrier
+    unsigned long long tl[7] = {0, 0, 0, 0, 0, 0, 0};
     if (tid == 0) {
         stamp_min(a.ts);
         mbar_init(&sm.bar, 1);
+        mbar_init(&sm.merge_bar, 1);
         mbar_fence_init();
+        // rank 0 expects C partials of n_rep * (128 + 2) floats
+        if (cluster_ctarank() == 0) mbar_expect_tx(&sm.merge_bar, (uint32_t)(C * n_rep * 130 * 4));
         sm.err = 0;
     }
     __syncthreads();
@@ -162,10 +177,23 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     }
     pdl_trigger();
     __syncthreads();
+    tl[0] = a.ts ? globaltimer_ns() : 0;
 
     // ---- rounds of up to ATC_PMAX cached positions (+ p_new in the last)
-    const int hh = tid >> 7, d = tid & 127;  // P.V: thread (head hh, dim d)
-    float o_run = 0.f;
+    // Scores: lane 8G+t of a warp works on slot i0+G and float4 columns
+    // t, t+8, t+16, t+24 of the K row (each 8-lane phase of a 128-bit shared
+    // load reads 128 contiguous bytes: no bank conflicts), reduced over the
+    // 8 lanes by 3 shuffles.  P.V: thread (group gp, head ph, float4 column
+    // pc) accumulates slots i = gp mod 4; the 4 group sums are added at the end.
+    const int sg = lane >> 3, st8 = lane & 7;
+    float4 qa[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            qa[h][j] = reinterpret_cast<const float4*>(sm.q[h < n_rep ? h : 0])[st8 + 8 * j];
+    const int pc = tid & 31, ph = (tid >> 5) & 1, gp = tid >> 6;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     uint32_t phase = 0;
     for (int rd = 0; rd < n_rounds; ++rd) {
@@ -181,28 +209,37 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             if (!mbar_wait(&sm.bar, phase, a.err)) sm.err = 1;
             phase ^= 1u;
         }
-        // scores: warp w takes slots w*4 .. w*4+3, then +32; 4 slots x 2 heads
-        // per butterfly (lane group l>>2 ends with value (slot l>>3, head (l>>2)&1))
-        const float4 q0 = reinterpret_cast<const float4*>(sm.q[0])[lane];
-        const float4 q1 = reinterpret_cast<const float4*>(sm.q[n_rep > 1 ? 1 : 0])[lane];
+        if (rd == 0) tl[1] = a.ts ? globaltimer_ns() : 0;
         for (int i0 = warp * 4; i0 < ns; i0 += 32) {
-            float vals[8];
+            const int i = i0 + sg;
+            const float4* kr = reinterpret_cast<const float4*>(i < nc ? sm.k[i < nc ? i : 0] : sm.kn);
+            float s0 = 0.f, s1 = 0.f;
+            if (i < ns) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int i = i0 + j;
-                float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (i < nc) kv = reinterpret_cast<const float4*>(sm.k[i])[lane];
-                else if (i < ns) kv = reinterpret_cast<const float4*>(sm.kn)[lane];
-                vals[2 * j] = q0.x * kv.x + q0.y * kv.y + q0.z * kv.z + q0.w * kv.w;
-                vals[2 * j + 1] = q1.x * kv.x + q1.y * kv.y + q1.z * kv.z + q1.w * kv.w;
+                for (int j = 0; j < 4; ++j) {
+                    const float4 kv = kr[st8 + 8 * j];
+                    s0 = fmaf(qa[0][j].x, kv.x, s0);
+                    s0 = fmaf(qa[0][j].y, kv.y, s0);
+                    s0 = fmaf(qa[0][j].z, kv.z, s0);
+                    s0 = fmaf(qa[0][j].w, kv.w, s0);
+                    s1 = fmaf(qa[1][j].x, kv.x, s1);
+                    s1 = fmaf(qa[1][j].y, kv.y, s1);
+                    s1 = fmaf(qa[1][j].z, kv.z, s1);
+                    s1 = fmaf(qa[1][j].w, kv.w, s1);
+                }
             }
-            const float res = butterfly_reduce<8>(vals, lane);
-            if ((lane & 3) == 0) {
-                const int vi = lane >> 2, i = i0 + (vi >> 1), h = vi & 1;
-                if (i < ns && h < n_rep) sm.p[h][i] = res;
+#pragma unroll
+            for (int o = 4; o >= 1; o >>= 1) {
+                s0 += __shfl_xor_sync(FULL, s0, o);
+                s1 += __shfl_xor_sync(FULL, s1, o);
+            }
+            if (st8 == 0 && i < ns) {
+                sm.p[0][i] = s0;
+                if (n_rep > 1) sm.p[1][i] = s1;
             }
         }
         __syncthreads();
+        if (rd == 0) tl[2] = a.ts ? globaltimer_ns() : 0;
         // per-head max (warp h), then probabilities and their sum (warp h)
         if (warp < n_rep) {
             float mx = -INFINITY;
@@ -222,70 +259,93 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             }
         }
         __syncthreads();
+        if (rd == 0) tl[3] = a.ts ? globaltimer_ns() : 0;
         // online update of (m, l, o) and P.V over this round's slots
-        float mnew[2], corr[2];
+        float corr[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            mnew[h] = h < n_rep ? sm.mr[h] : -INFINITY;
-            corr[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew[h]);
+            const float mnew = h < n_rep ? sm.mr[h] : -INFINITY;
+            corr[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew);
             l_run[h] = l_run[h] * corr[h] + (h < n_rep ? sm.lr[h] : 0.f);
-            m_run[h] = mnew[h];
+            m_run[h] = mnew;
         }
-        if (hh < n_rep) {
-            float acc = o_run * corr[hh];
-            const float* pr = sm.p[hh];
-            int i = 0;
-            for (; i + 4 <= nc; i += 4) {
-                acc = fmaf(pr[i], sm.v[i][d], acc);
-                acc = fmaf(pr[i + 1], sm.v[i + 1][d], acc);
-                acc = fmaf(pr[i + 2], sm.v[i + 2][d], acc);
-                acc = fmaf(pr[i + 3], sm.v[i + 3][d], acc);
+        if (ph < n_rep) {
+            const float c = corr[ph];
+            acc = make_float4(acc.x * c, acc.y * c, acc.z * c, acc.w * c);
+            const float* pr = sm.p[ph];
+            for (int i = gp; i < ns; i += 4) {
+                const float pi = pr[i];
+                const float4 vv = reinterpret_cast<const float4*>(i < nc ? sm.v[i < nc ? i : 0] : sm.vn)[pc];
+                acc.x = fmaf(pi, vv.x, acc.x);
+                acc.y = fmaf(pi, vv.y, acc.y);
+                acc.z = fmaf(pi, vv.z, acc.z);
+                acc.w = fmaf(pi, vv.w, acc.w);
             }
-            for (; i < nc; ++i) acc = fmaf(pr[i], sm.v[i][d], acc);
-            if (ns > nc) acc = fmaf(pr[nc], sm.vn[d], acc);
-            o_run = acc;
         }
         __syncthreads();  // sm.k / sm.v / sm.p are refilled by the next round
     }
+    // the 4 slot groups' sums, added in group order (K buffer as scratch)
+    float* gsum = &sm.k[0][0];  // [4][2][128]
+    if (ph < n_rep) reinterpret_cast<float4*>(gsum + (gp * 2 + ph) * 128)[pc] = acc;
+    __syncthreads();
+    const int hh = tid >> 7, d = tid & 127;  // merge: thread (head hh, dim d)
+    float o_run = 0.f;
+    if (hh < n_rep)
+        o_run = ((gsum[(0 * 2 + hh) * 128 + d] + gsum[(1 * 2 + hh) * 128 + d]) + gsum[(2 * 2 + hh) * 128 + d]) +
+                gsum[(3 * 2 + hh) * 128 + d];
+    tl[4] = a.ts ? globaltimer_ns() : 0;
 
-    // ---- merge: once every CTA of the cluster is done with its K/V buffers,
-    // each pushes its partial (max, sum, output) into rank 0's K buffer with
-    // remote stores; after a second cluster barrier rank 0 merges them in
-    // split order from its own shared memory.
+    // ---- merge: once every CTA of the cluster is done with its K/V buffers
+    // (an execution-only cluster barrier, which also publishes rank 0's merge
+    // barrier initialised at the start), each sends its partial (output, max,
+    // sum) into rank 0's K buffer with asynchronous remote stores that count
+    // down rank 0's merge barrier; rank 0 merges them in split order.
     if (tid == 0 && sm.err) {
         // a copy did not arrive in time: flag it and wait (bounded) once more
         // so that no copy is still in flight when the buffers are reused
         if (a.err != nullptr) atomicExch(a.err, 1);
         mbar_wait(&sm.bar, phase ^ 1u, nullptr);
     }
-    cluster_sync_all();
+    __syncthreads();  // the group sums in the K buffer are read
+    cluster_sync_exec();
+    tl[5] = a.ts ? globaltimer_ns() : 0;
     const uint32_t rank = cluster_ctarank();
     float* slot = &sm.k[0][0] + (size_t)rank * ATC_PART;  // [2][128] o | [2] m | [2] l
     if (hh < n_rep) {
-        st_dsmem(slot + hh * 128 + d, o_run, 0);
+        st_async_f32(slot + hh * 128 + d, o_run, &sm.merge_bar, 0);
         if (d == 0) {
-            st_dsmem(slot + 256 + hh, m_run[hh], 0);
-            st_dsmem(slot + 258 + hh, l_run[hh], 0);
+            st_async_f32(slot + 256 + hh, m_run[hh], &sm.merge_bar, 0);
+            st_async_f32(slot + 258 + hh, l_run[hh], &sm.merge_bar, 0);
         }
     }
-    cluster_sync_all();
     if (rank == 0 && hh < n_rep) {
-        const float* parts = &sm.k[0][0];
-        float M = -INFINITY;
-        for (int j = 0; j < C; ++j) M = fmaxf(M, parts[j * ATC_PART + 256 + hh]);
-        float L = 0.f, O = 0.f;
-        for (int j = 0; j < C; ++j) {
-            const float* pj = parts + j * ATC_PART;
-            const float mj = pj[256 + hh];
-            const float w = (mj == -INFINITY) ? 0.f : expf(mj - M);
-            L = fmaf(pj[258 + hh], w, L);
-            O = fmaf(pj[hh * 128 + d], w, O);
+        const bool ok = mbar_wait(&sm.merge_bar, 0, a.err);
+        tl[6] = a.ts ? globaltimer_ns() : 0;
+        if (ok) {
+            const float* parts = &sm.k[0][0];
+            float M = -INFINITY;
+            for (int j = 0; j < C; ++j) M = fmaxf(M, parts[j * ATC_PART + 256 + hh]);
+            float L = 0.f, O = 0.f;
+            for (int j = 0; j < C; ++j) {
+                const float* pj = parts + j * ATC_PART;
+                const float mj = pj[256 + hh];
+                const float w = (mj == -INFINITY) ? 0.f : expf(mj - M);
+                L = fmaf(pj[258 + hh], w, L);
+                O = fmaf(pj[hh * 128 + d], w, O);
+            }
+            a.out[(size_t)r * a.H * 128 + (g * n_rep + hh) * 128 + d] = O / L;
         }
-        a.out[(size_t)r * a.H * 128 + (g * n_rep + hh) * 128 + d] = O / L;
     }
+    // rank 0 arrives once every partial has landed, so no CTA exits with one
+    // of its remote stores still in flight
+    cluster_sync_exec();
     if (a.ts) {
         __syncthreads();
-        if (tid == 0) stamp_max(a.ts + 3);
+        if (tid == 0) {
+            stamp_max(a.ts + 3);
+#pragma unroll
+            for (int k = 0; k < 7; ++k) atomicMax(a.ts + 4 + k, tl[k]);
+        }
     }
 }
 

@@ -131,10 +131,15 @@ __device__ __forceinline__ float butterfly_reduce(float (&v)[N], int lane) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
-// Barrier policy of the block-wide building blocks (sampler, attention item):
-// every thread of the CTA takes part.
+// Barrier policies of the block-wide building blocks (sampler, attention
+// item).  BlockSync: every thread of the CTA takes part.
 struct BlockSync {
     __device__ __forceinline__ static void sync() { __syncthreads(); }
+};
+// The same for code run by the 256 threads of warps 0..7 of a CTA whose other
+// warps have exited or run independently: named barrier 1.
+struct ConsumerSync {
+    __device__ __forceinline__ static void sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 };
 
 // ------------------------------------------------------ bulk copy + mbarrier
@@ -191,8 +196,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // --------------------------------------------------------- kernel stamps
 // Debug timeline of one launch (all null unless the engine's debug mode is
-// on): ts[0] earliest CTA start, ts[1] earliest and ts[2] latest release from
-// the programmatic-dependent-launch wait, ts[3] latest CTA end (%globaltimer ns).
+// on), SKB_KTS_STRIDE slots: ts[0] earliest CTA start, ts[1] earliest and
+// ts[2] latest release from the programmatic-dependent-launch wait, ts[3]
+// latest CTA end, ts[4..] latest CTA to reach kernel-specific points
+// (%globaltimer ns).
+constexpr int SKB_KTS_STRIDE = 16;
 __device__ __forceinline__ void stamp_min(unsigned long long* p) {
     if (p) atomicMin(p, (unsigned long long)globaltimer_ns());
 }

@@ -34,6 +34,9 @@
 
 namespace skb {
 
+// VMAX: audio vocabulary capacity (2304 covers soraku's 2051 codes with 9
+// logits per thread).
+template <int VMAX>
 __global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const DepthSampleArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int codes_s[32];
@@ -42,7 +45,7 @@ __global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const Dep
     pdl_wait();
     if (threadIdx.x == 0) stamp_wait(a.ts);
     pdl_trigger();
-    depth_sample_body<BlockSync, SAMPLER_VMAX>(a, blockIdx.x, smem, codes_s);
+    depth_sample_body<BlockSync, VMAX>(a, blockIdx.x, smem, codes_s);
     if (a.ts) {
         __syncthreads();
         if (threadIdx.x == 0) stamp_max(a.ts + 3);
@@ -80,7 +83,7 @@ struct skb_engine {
     cudaGraphExec_t exec = nullptr;
     int graph_active = 0, graph_fpg = 0, graph_pdl = 0;
     int debug = 0;
-    unsigned long long* kts = nullptr;  // debug kernel timeline [kernels per frame][4]
+    unsigned long long* kts = nullptr;  // debug kernel timeline [kernels per frame][SKB_KTS_STRIDE]
     std::vector<int> frames_host, pos_host;
     std::vector<ReqState> st_host;
     std::vector<void*> allocs;
@@ -337,7 +340,7 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
 std::vector<Node> build_frame(skb_engine* e, int n_active) {
     const int R = n_active * e->rpr;
     std::vector<Node> nodes;
-    auto stamps = [e, &nodes]() { return e->debug ? e->kts + 4 * nodes.size() : nullptr; };
+    auto stamps = [e, &nodes]() { return e->debug ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr; };
     for (const Phase& ph : build_phases(e, n_active)) {
         if (ph.kind == PH_GEMV) {
             GemvArgs g = ph.g;
@@ -351,7 +354,11 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
                 n.run = [a, n_active](cudaStream_t s, bool pdl, const PrefetchList& pf) {
                     DepthSampleArgs b = a;
                     b.pf = pf;
-                    return launch(depth_sample_kernel, dim3(n_active), dim3(SAMPLER_THREADS), SAMPLER_SMEM, s, pdl, b);
+                    if (b.V <= DEPTH_VMAX_SMALL)
+                        return launch(depth_sample_kernel<DEPTH_VMAX_SMALL>, dim3(n_active), dim3(SAMPLER_THREADS),
+                                      sampler_smem_bytes<DEPTH_VMAX_SMALL>(), s, pdl, b);
+                    return launch(depth_sample_kernel<SAMPLER_VMAX>, dim3(n_active), dim3(SAMPLER_THREADS),
+                                  sampler_smem_bytes<SAMPLER_VMAX>(), s, pdl, b);
                 };
                 nodes.push_back(n);
             }
@@ -515,7 +522,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->pos, e->R)
     A(e->page_table, (size_t)e->R * e->max_pages)
     A(e->err, 8)
-    A(e->kts, (size_t)4 * (e->Q * 4 + e->L * 5))
+    A(e->kts, (size_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5))
     A(e->host_flag, 1)
     A(e->cur_codes, (size_t)e->nreq * e->Q)
     A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
@@ -570,7 +577,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
         skb_engine_destroy(e);
         return fail(SKB_ERR_CUDA, "stream creation failed");
     }
-    set_smem_attrs(depth_sample_kernel, SAMPLER_SMEM);
+    set_smem_attrs(depth_sample_kernel<DEPTH_VMAX_SMALL>, sampler_smem_bytes<DEPTH_VMAX_SMALL>());
+    set_smem_attrs(depth_sample_kernel<SAMPLER_VMAX>, sampler_smem_bytes<SAMPLER_VMAX>());
     decode_attn_cluster_prepare();
     trunk_init_attrs();
     gemv_prepare_all();
@@ -887,7 +895,7 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
         case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
-        case 8: *ptr = e->kts; *numel = (int64_t)4 * skb_engine_kernels_per_frame(e); break;
+        case 8: *ptr = e->kts; *numel = (int64_t)SKB_KTS_STRIDE * skb_engine_kernels_per_frame(e); break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }
     return SKB_OK;

@@ -57,7 +57,12 @@ __device__ void depth_sample_body(const DepthSampleArgs& a, int r, unsigned char
     J.pad = a.pad;
     J.eos = a.eos;
     J.u = philox_uniform(st->seed, (uint32_t)r, (uint32_t)frame, (uint32_t)a.q);
+    J.ts = a.ts;
+    J.pf_rows = a.table + (size_t)a.q * a.V * a.D;
+    J.row_floats = a.D;
+    if (tid == 0 && a.ts) stamp_max(a.ts + 4);
     const int code = sample_one<Sync, VMAX>(J, smem);
+    if (tid == 0 && a.ts) stamp_max(a.ts + 11);
     if (tid == 0) {
         a.cur_codes[(size_t)r * a.Q + a.q] = code;
         if (frame < a.max_frames) a.hist[((size_t)r * a.max_frames + frame) * a.Q + a.q] = code;

@@ -18,7 +18,7 @@ static cudaError_t gemv_go(const GemvArgs& a, const RgPlan& p, cudaStream_t s, b
     constexpr bool XR = (KQ == 8 && GEMV_M <= 2);
     auto kern = rgemv_kernel<GEMV_M, KQ, XMV, EMV, XR>;
     if (p.grid <= 0)  // prepare only
-        return set_smem_attrs(kern, RG_SMEM_BUDGET);
+        return set_smem_attrs(kern, RG_SMEM_MAX);
     return launch(kern, dim3(p.grid), dim3(RG_THREADS), p.smem, s, pdl, a, p.slots);
 }
 

@@ -37,8 +37,13 @@ constexpr int RG_SLOT = 24 * 1024;                // ring slot bytes
 constexpr int RG_MAX_SLOTS = 4;
 constexpr int RG_HEAD = 256;                      // mbarriers + flags
 // Dynamic shared memory per CTA: at most this much, so that two CTAs (of this
-// kernel and the next) fit in one SM's 228 KB.
+// kernel and its neighbour in the frame) fit in one SM's 228 KB.  Inner size
+// 3072 (the trunk down projection, a 12 KB row) gets room for a fourth slot:
+// its whole slice (7 rows at bs1) is then staged before the wait, and its
+// neighbours (gate/up, QKV: 104 KB each) still fit beside it.
 constexpr size_t RG_SMEM_BUDGET = 112 * 1024;
+constexpr size_t RG_SMEM_BUDGET_K3072 = 121 * 1024;
+constexpr size_t RG_SMEM_MAX = RG_SMEM_BUDGET_K3072;
 constexpr int RG_EPI_MAX = 256;  // staged residual / bias values per CTA
 
 struct RgHead {
@@ -87,11 +92,13 @@ __device__ __forceinline__ void rg_issue(const GemvArgs& a, bool swiglu, int upc
 }
 
 // KQ: float4 columns per lane (K <= 128 * KQ).  XR: activations in registers.
+// rsm: the kernel's dynamic shared memory.  Returns false in the producer
+// warp (which is done once it has issued every copy), true in the consumer
+// warps once this CTA's outputs are stored.
 template <int M, int KQ, int XM, int EM, bool XR>
-__global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots) {
+__device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, unsigned char* rsm) {
     constexpr bool SW = (EM == E_SWIGLU);
     constexpr int KP4 = KQ * 32;  // padded float4 columns per activation row
-    extern __shared__ __align__(128) unsigned char rsm[];
     RgHead& hd = *reinterpret_cast<RgHead*>(rsm);
     float4* xs = reinterpret_cast<float4*>(rsm + RG_HEAD);  // [M][KP4]
     float* ring = reinterpret_cast<float*>(rsm + RG_HEAD + (size_t)M * KP4 * 16);
@@ -136,7 +143,7 @@ __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots)
             __threadfence_block();
             *(volatile int*)&hd.producer_done = 1;
         }
-        return;
+        return false;
     }
 
     // ----------------------------------------------------------- consumers
@@ -267,6 +274,7 @@ __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots)
     // launch now (its weight burst no longer delays the round trip above).
     pdl_trigger();
     named_sync_consumers();
+    if (tid == 0 && a.ts) stamp_max(a.ts + 4);
     float4 xv[XR ? M : 1][XR ? KQ : 1];
     if (XR) {
 #pragma unroll
@@ -357,6 +365,20 @@ __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots)
         const unsigned first = issued > (unsigned)S ? issued - (unsigned)S : 0u;
         for (unsigned k = first; k < issued; ++k) mbar_wait(&hd.full[k % S], (k / S) & 1u, nullptr);
     }
+    return true;
+}
+
+template <int M, int KQ, int XM, int EM, bool XR>
+__global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots) {
+    extern __shared__ __align__(128) unsigned char rsm[];
+    rgemv_body<M, KQ, XM, EM, XR>(a, slots, rsm);
+}
+
+// Offset of the weight ring in the dynamic shared memory (the region a kernel
+// may reuse once every chunk has been consumed).
+template <int M, int KQ>
+__host__ __device__ constexpr size_t rgemv_ring_offset() {
+    return RG_HEAD + (size_t)M * KQ * 128 * 4;
 }
 
 // ------------------------------------------------------------------ host
@@ -377,7 +399,8 @@ inline RgPlan rgemv_plan(int N, int K, int M, int EM, int want) {
     p.kq = K <= 1024 ? 8 : (K <= 2048 ? 16 : 24);
     p.xr = (p.kq == 8 && M <= 2);
     const size_t xbytes = (size_t)M * p.kq * 128 * 4;
-    const size_t avail = RG_SMEM_BUDGET - RG_HEAD - xbytes;
+    const size_t budget = p.kq == 24 ? RG_SMEM_BUDGET_K3072 : RG_SMEM_BUDGET;
+    const size_t avail = budget > RG_HEAD + xbytes + 2 * RG_SLOT ? budget - RG_HEAD - xbytes : 2 * RG_SLOT;
     p.slots = (int)(avail / RG_SLOT);
     if (p.slots > RG_MAX_SLOTS) p.slots = RG_MAX_SLOTS;
     if (p.slots < 2) p.slots = 2;

@@ -33,6 +33,7 @@ namespace skb {
 constexpr int SAMPLER_THREADS = 256;
 constexpr int SAMPLER_VMAX = 4096;
 constexpr int SAMPLER_BINS = 2048;
+constexpr int DEPTH_VMAX_SMALL = 2304;
 
 // Dynamic shared memory layout of the sampler (bytes).
 constexpr size_t SAMPLER_SMEM = (size_t)SAMPLER_VMAX * 8  // f (floats), then sorted keys (u64)
@@ -118,6 +119,12 @@ struct SampleJob {
     float cfg_scale, temperature, top_p;
     int top_k, mask_eos, bos, pad, eos;
     float u;
+    unsigned long long* ts;  // optional debug stage stamps (slots 6..11 of a kernel timeline)
+    // optional: rows of `row_floats` floats indexed by code, of which the
+    // candidates' rows are prefetched into L2 once the top-k set is known
+    // (the caller reads the drawn code's row right after the draw)
+    const float* pf_rows;
+    int row_floats;
 };
 
 // Block-wide exclusive scan of one int per thread (256 threads).
@@ -188,6 +195,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         fv[k] = m;
     }
 
+    if (tid == 0 && J.ts) stamp_max(J.ts + 6);
     if (greedy) {
         // first maximal index
         float bv = -INFINITY;
@@ -266,6 +274,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         Sync::sync();
         low_key = (uint32_t)sc[9] << 21;
     }
+    if (tid == 0 && J.ts) stamp_max(J.ts + 7);
     // compaction of every element at or above the cutoff bin: slots come from a
     // block scan of per-thread counts (the rank sort below fixes the order)
     int mine = 0;
@@ -291,6 +300,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         sorted[rank] = ki;
     }
     Sync::sync();
+    if (tid == 0 && J.ts) stamp_max(J.ts + 8);
     // top-k: keep the sorted prefix with f >= cutoff (ties kept); its end is the
     // one position where f >= cutoff is followed by f < cutoff (or the end)
     int n = C;
@@ -304,10 +314,15 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         Sync::sync();
         n = sc[10];
     }
+    if (J.pf_rows != nullptr && tid < n && tid < 64) {
+        const uint32_t idx = 0xffffffffu - (uint32_t)(sorted[tid] & 0xffffffffull);
+        bulk_prefetch_l2(J.pf_rows + (size_t)idx * J.row_floats, (unsigned)J.row_floats * 4u);
+    }
     const float top = key_float((uint32_t)(sorted[0] >> 32));
     for (int j = tid; j < n; j += SAMPLER_THREADS)
         e[j] = skb_exp(__fsub_rn(key_float((uint32_t)(sorted[j] >> 32)), top));
     Sync::sync();
+    if (tid == 0 && J.ts) stamp_max(J.ts + 9);
     // Sequential FP32 sums in candidate order (thread 0), as the oracle does;
     // operands are read 8 at a time ahead of the dependent adds.
     const bool topp_on = J.top_p > 0.0f && J.top_p < 1.0f;
@@ -353,6 +368,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         sc[11] = n;
     }
     Sync::sync();
+    if (tid == 0 && J.ts) stamp_max(J.ts + 10);
     if (tid == 0) {
         const int keep = sc[11];
         float s2 = 0.0f;
