@@ -208,7 +208,7 @@ def kernel_only_main(args):
     k_ms, k_bytes = time_gateup_kernel(params, n_layers)
     peak, peak_kind = measured_peak_hbm()
     gbs = k_bytes / (k_ms * 1e-3) / 1e9
-    print(json.dumps({"kernel": "gemv_kernel swiglu M=2 3072x1024", "launch_ms": round(k_ms, 5),
+    print(json.dumps({"kernel": "rgemv_kernel swiglu M=2 3072x1024", "launch_ms": round(k_ms, 5),
                       "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_kind": peak_kind}), flush=True)
     return 0
 
@@ -399,7 +399,7 @@ def b200_main(args, wl):
         "e2e": {"value": round(e2e, 3), "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(k_gbs / peak, 4), "traffic": profiled_traffic(),
-                     "kernel": "gemv_kernel (trunk gate/up SwiGLU GEMV, M=2, 25.2 MB weights/launch)",
+                     "kernel": "rgemv_kernel (trunk gate/up SwiGLU GEMV, M=2, 25.2 MB weights/launch)",
                      "peak_kind": peak_kind, "launch_ms": round(k_ms, 5), "bytes_per_launch": k_bytes},
         "roofline_frame": {"bound": "hbm", "achieved": round(f_gbs, 1), "peak": peak, "unit": "GB/s",
                            "frac": round(f_gbs / peak, 4), "bytes_per_frame": int(bpf), "peak_kind": peak_kind},

@@ -43,6 +43,8 @@ int skb_abi_version(void);
 /* ------------------------------------------------------------------------
  * Op surface.  Same names, argument order and meaning as the TileLang
  * factories; the factory's static shape parameters become size arguments.
+ * GEMV inner sizes (D of swiglu/classifier, I of down) must be multiples of
+ * 4 and <= 3072; pointers 16-byte aligned (SKB_ERR_ARG otherwise).
  * ---------------------------------------------------------------------- */
 
 /* tilelang_kernels.py:34-55  add_rmsnorm(B,D,eps)(hidden,prefix,weight)

@@ -42,10 +42,12 @@ __global__ void __launch_bounds__(SAMPLER_THREADS) depth_sample_kernel(const Dep
     __shared__ int codes_s[32];
     if (threadIdx.x == 0) stamp_min(a.ts);
     prefetch_share(a.pf, blockIdx.x, gridDim.x);
+    int frame;
+    const SampleJob J = depth_sample_job(a, blockIdx.x, &frame);
     pdl_wait();
     if (threadIdx.x == 0) stamp_wait(a.ts);
     pdl_trigger();
-    depth_sample_body<BlockSync, VMAX>(a, blockIdx.x, smem, codes_s);
+    depth_sample_body<BlockSync, VMAX>(a, blockIdx.x, J, frame, smem, codes_s);
     if (a.ts) {
         __syncthreads();
         if (threadIdx.x == 0) stamp_max(a.ts + 3);
@@ -443,9 +445,11 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     if (m.head_dim != 128) return fail(SKB_ERR_ARG, "head_dim must be 128 (got %d)", m.head_dim);
     if (m.n_heads % m.n_kv_heads != 0 || m.n_heads / m.n_kv_heads > 2)
         return fail(SKB_ERR_ARG, "GQA group size must be 1 or 2 (heads %d / kv heads %d)", m.n_heads, m.n_kv_heads);
-    if (m.d_model % 16 || m.d_model > 4096 || m.ffn_dim % 16 || m.ffn_dim > 4096 || m.depth_inner % 16 ||
-        m.depth_inner > 4096 || m.n_heads * m.head_dim > 4096)
-        return fail(SKB_ERR_ARG, "model widths must be multiples of 16 and <= 4096");
+    // every GEMV inner size must fit the ring GEMV (K <= 3072: a SwiGLU row
+    // pair fills one 24 KB slot)
+    if (m.d_model % 16 || m.d_model > 3072 || m.ffn_dim % 16 || m.ffn_dim > 3072 || m.depth_inner % 16 ||
+        m.depth_inner > 3072 || m.n_heads * m.head_dim > 3072)
+        return fail(SKB_ERR_ARG, "model widths must be multiples of 16 and <= 3072");
     if (m.audio_vocab > SAMPLER_VMAX) return fail(SKB_ERR_ARG, "audio vocab %d > %d", m.audio_vocab, SAMPLER_VMAX);
     if (m.n_codebooks > 32 || m.n_codebooks < 1) return fail(SKB_ERR_ARG, "1..32 codebooks supported");
     if (opts->rows_per_request != 1 && opts->rows_per_request != 2)

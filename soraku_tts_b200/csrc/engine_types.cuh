@@ -32,16 +32,12 @@ struct DepthSampleArgs {
     unsigned long long* ts;  // optional debug timeline [4]
 };
 
-// One request's sampling step for codebook a.q and its epilogue: the code goes
-// to the current-frame and history buffers, the prefix grows by
-// table[q][code] * scale, and after the last codebook the frame embedding
-// (sum over q in order, then * scale) becomes both CFG rows' residual stream,
-// the prefix is cleared and the request's frame counter advances.
-// Threads 0..255 take part.  codes_s: 32 ints of shared memory.
-template <class Sync, int VMAX>
-__device__ void depth_sample_body(const DepthSampleArgs& a, int r, unsigned char* smem, int* codes_s) {
-    const int tid = threadIdx.x;
-    ReqState* st = a.st + r;
+// The sampling job of request r for codebook a.q.  It reads only the
+// request's state and the host EOS flag, which no kernel of the current
+// frame writes before the sampler, so a kernel may build it before its
+// programmatic-dependent-launch wait.
+__device__ __forceinline__ SampleJob depth_sample_job(const DepthSampleArgs& a, int r, int* frame_out) {
+    const ReqState* st = a.st + r;
     const int frame = __ldcg(&st->frame);
     const bool q0 = a.q == 0;
     SampleJob J;
@@ -60,6 +56,22 @@ __device__ void depth_sample_body(const DepthSampleArgs& a, int r, unsigned char
     J.ts = a.ts;
     J.pf_rows = a.table + (size_t)a.q * a.V * a.D;
     J.row_floats = a.D;
+    *frame_out = frame;
+    return J;
+}
+
+// One request's sampling step for codebook a.q (job J from depth_sample_job)
+// and its epilogue: the code goes to the current-frame and history buffers,
+// the prefix grows by table[q][code] * scale, and after the last codebook the
+// frame embedding (sum over q in order, then * scale) becomes both CFG rows'
+// residual stream, the prefix is cleared and the request's frame counter
+// advances.  Threads 0..255 take part.  codes_s: 32 ints of shared memory.
+template <class Sync, int VMAX>
+__device__ void depth_sample_body(const DepthSampleArgs& a, int r, const SampleJob& J, int frame,
+                                  unsigned char* smem, int* codes_s) {
+    const int tid = threadIdx.x;
+    ReqState* st = a.st + r;
+    const bool q0 = a.q == 0;
     if (tid == 0 && a.ts) stamp_max(a.ts + 4);
     const int code = sample_one<Sync, VMAX>(J, smem);
     if (tid == 0 && a.ts) stamp_max(a.ts + 11);
@@ -76,13 +88,18 @@ __device__ void depth_sample_body(const DepthSampleArgs& a, int r, unsigned char
         if (tid < a.Q) codes_s[tid] = (tid == a.q) ? code : (int)__ldcg(a.cur_codes + (size_t)r * a.Q + tid);
         Sync::sync();
         for (int i = tid; i < a.D; i += SAMPLER_THREADS) {
-            float acc = 0.f;
-            for (int qq = 0; qq < a.Q; ++qq) {
-                int c = codes_s[qq];
+            // all codebooks' rows are requested before the in-order sum
+            float v[32];
+#pragma unroll
+            for (int qq = 0; qq < 32; ++qq) {
+                int c = qq < a.Q ? codes_s[qq] : 0;
                 if (c < 0 || c >= a.V) c = 0;
-                const float v = a.table[((size_t)qq * a.V + c) * a.D + i];
-                acc = (qq == 0) ? v : acc + v;
+                v[qq] = qq < a.Q ? a.table[((size_t)qq * a.V + c) * a.D + i] : 0.f;
             }
+            float acc = v[0];
+#pragma unroll
+            for (int qq = 1; qq < 32; ++qq)
+                if (qq < a.Q) acc = acc + v[qq];
             acc = acc * a.scale;
             for (int rr = 0; rr < a.rows_per_req; ++rr) a.x[((size_t)r * a.rows_per_req + rr) * a.D + i] = acc;
             pr[i] = 0.f;

@@ -247,8 +247,8 @@ int skb_rmsnorm(const float* x, const float* weight, float* out, int B, int D, f
 static int check_gemv_shapes(const char* what, int B, int N, int K, const void* p0, const void* p1,
                              const void* p2, const void* p3) {
     if (B < 0 || N <= 0 || K <= 0) return fail(SKB_ERR_ARG, "%s: bad sizes B=%d N=%d K=%d", what, B, N, K);
-    if (K % 4 != 0 || K > 4096)
-        return fail(SKB_ERR_ARG, "%s: inner size %d must be a multiple of 4 and <= 4096", what, K);
+    if (K % 4 != 0 || K > 3072)
+        return fail(SKB_ERR_ARG, "%s: inner size %d must be a multiple of 4 and <= 3072", what, K);
     const void* ps[4] = {p0, p1, p2, p3};
     for (int i = 0; i < 4; ++i)
         if (ps[i] && !aligned16(ps[i])) return fail(SKB_ERR_ARG, "%s: pointer %d not 16-byte aligned", what, i);

@@ -35,11 +35,6 @@ constexpr int SAMPLER_VMAX = 4096;
 constexpr int SAMPLER_BINS = 2048;
 constexpr int DEPTH_VMAX_SMALL = 2304;
 
-// Dynamic shared memory layout of the sampler (bytes).
-constexpr size_t SAMPLER_SMEM = (size_t)SAMPLER_VMAX * 8  // f (floats), then sorted keys (u64)
-                                + (size_t)SAMPLER_VMAX * 8  // candidates (u64), then e (floats)
-                                + SAMPLER_BINS * 4          // histogram
-                                + 256;                      // scalars
 
 // ---------------------------------------------------------------- exp
 // Cody-Waite reduction + degree-7 Taylor polynomial (W. J. Cody and W. Waite,
@@ -152,10 +147,13 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp /* [8] */, i
 }
 
 // Shared memory a sampler with vocabulary capacity VMAX needs.
+// [sorted keys: VMAX u64][candidates, then e and running sums: VMAX u64]
+// [histogram][scalars][e / S1: VMAX floats]
 template <int VMAX>
 constexpr size_t sampler_smem_bytes() {
-    return (size_t)VMAX * 16 + SAMPLER_BINS * 4 + 256;
+    return (size_t)VMAX * 20 + SAMPLER_BINS * 4 + 256;
 }
+constexpr size_t SAMPLER_SMEM = sampler_smem_bytes<SAMPLER_VMAX>();
 
 // Returns the drawn code (same value in every thread).  smem:
 // sampler_smem_bytes<VMAX>() bytes of shared memory, 16-byte aligned.
@@ -323,87 +321,84 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         e[j] = skb_exp(__fsub_rn(key_float((uint32_t)(sorted[j] >> 32)), top));
     Sync::sync();
     if (tid == 0 && J.ts) stamp_max(J.ts + 9);
-    // Sequential FP32 sums in candidate order (thread 0), as the oracle does;
-    // operands are read 8 at a time ahead of the dependent adds.
+    // Sequential FP32 sums in candidate order, as the oracle does.  One pass
+    // (thread 0) forms the running sums P_j = e_0 + ... + e_j in order: the
+    // oracle's S1 is P_{n-1}, its S2 is P_{keep-1} and its draw compares the
+    // same running sums, so those need no pass of their own.
+    float* P = e + VMAX;  // running sums, then (top-p) e_j / S1 after them
+    if (tid == 0) {
+        float run = 0.0f;
+        for (int j0 = 0; j0 < n; j0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? e[j0 + t] : 0.f;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (j0 + t < n) {
+                    run = __fadd_rn(run, v[t]);
+                    P[j0 + t] = run;
+                }
+            }
+        }
+        sc[11] = n;
+    }
+    Sync::sync();
     const bool topp_on = J.top_p > 0.0f && J.top_p < 1.0f;
     if (topp_on) {
-        if (tid == 0) {
-            float s1 = 0.0f;
-            for (int j0 = 0; j0 < n; j0 += 8) {
-                float v[8];
-#pragma unroll
-                for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? e[j0 + t] : 0.f;
-#pragma unroll
-                for (int t = 0; t < 8; ++t)
-                    if (j0 + t < n) s1 = __fadd_rn(s1, v[t]);
-            }
-            scf[0] = s1;
-        }
-        Sync::sync();
-        const float s1 = scf[0];
-        // e_j / S1 in parallel into the candidate area beyond e (floats)
-        float* pj = e + VMAX;
+        const float s1 = P[n - 1];
+        // e_j / S1 in parallel, then its sequential running sum (thread 0);
+        // the prefix is kept up to and including the first j with cum > p
+        float* pj = reinterpret_cast<float*>(smem + (size_t)VMAX * 16 + SAMPLER_BINS * 4 + 256);
         for (int j = tid; j < n; j += SAMPLER_THREADS) pj[j] = __fdiv_rn(e[j], s1);
         Sync::sync();
         if (tid == 0) {
-            // the whole running sum is formed (same adds in the same order as
-            // stopping at the first crossing) so the loads can run ahead
             int keep = n;
             float cum = 0.0f;
-            for (int j0 = 0; j0 < n; j0 += 8) {
+            for (int j0 = 0; j0 < n && keep == n; j0 += 8) {
                 float v[8];
 #pragma unroll
                 for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? pj[j0 + t] : 0.f;
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {
-                    if (j0 + t < n) {
+                    if (j0 + t < n && keep == n) {
                         cum = __fadd_rn(cum, v[t]);
-                        if (cum > J.top_p && keep == n) keep = j0 + t + 1;
+                        if (cum > J.top_p) keep = j0 + t + 1;
                     }
                 }
             }
             sc[11] = keep;
         }
-    } else if (tid == 0) {
-        sc[11] = n;
+        Sync::sync();
     }
-    Sync::sync();
-    if (tid == 0 && J.ts) stamp_max(J.ts + 10);
-    if (tid == 0) {
+    // draw: t = u * S2; the first kept j whose running sum exceeds t (else the
+    // last kept j with e_j > 0), found by a block-wide minimum / maximum
+    {
         const int keep = sc[11];
-        float s2 = 0.0f;
-        for (int j0 = 0; j0 < keep; j0 += 8) {
-            float v[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) v[t] = (j0 + t < keep) ? e[j0 + t] : 0.f;
-#pragma unroll
-            for (int t = 0; t < 8; ++t)
-                if (j0 + t < keep) s2 = __fadd_rn(s2, v[t]);
+        const float t = __fmul_rn(J.u, P[keep - 1]);
+        int first = 0x7fffffff, lastpos = -1;
+        for (int j = tid; j < keep; j += SAMPLER_THREADS) {
+            if (P[j] > t && j < first) first = j;
+            if (e[j] > 0.0f) lastpos = j;
         }
-        const float t = __fmul_rn(J.u, s2);
-        int pick = -1;
-        float run = 0.0f;
-        for (int j0 = 0; j0 < keep; j0 += 8) {
-            float v[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) v[q] = (j0 + q < keep) ? e[j0 + q] : 0.f;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                if (j0 + q < keep) {
-                    run = __fadd_rn(run, v[q]);
-                    if (run > t && pick < 0) pick = j0 + q;
-                }
+        for (int o = 16; o > 0; o >>= 1) {
+            first = min(first, __shfl_xor_sync(FULL, first, o));
+            lastpos = max(lastpos, __shfl_xor_sync(FULL, lastpos, o));
+        }
+        if ((tid & 31) == 0) {
+            sc[16 + (tid >> 5)] = first;
+            sc[24 + (tid >> 5)] = lastpos;
+        }
+        Sync::sync();
+        if (tid == 0) {
+            int f = 0x7fffffff, lp = -1;
+            for (int w = 0; w < SAMPLER_THREADS / 32; ++w) {
+                f = min(f, sc[16 + w]);
+                lp = max(lp, sc[24 + w]);
             }
+            const int pick = f != 0x7fffffff ? f : (lp >= 0 ? lp : 0);
+            sc[12] = (int)(0xffffffffu - (uint32_t)(sorted[pick] & 0xffffffffull));
         }
-        if (pick < 0) {
-            pick = 0;
-            for (int j = keep - 1; j >= 0; --j)
-                if (e[j] > 0.0f) {
-                    pick = j;
-                    break;
-                }
-        }
-        sc[12] = (int)(0xffffffffu - (uint32_t)(sorted[pick] & 0xffffffffull));
     }
     Sync::sync();
     if (n_kept_out) *n_kept_out = sc[11];
