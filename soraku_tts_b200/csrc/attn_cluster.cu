@@ -183,8 +183,9 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     // Scores: lane 8G+t of a warp works on slot i0+G and float4 columns
     // t, t+8, t+16, t+24 of the K row (each 8-lane phase of a 128-bit shared
     // load reads 128 contiguous bytes: no bank conflicts), reduced over the
-    // 8 lanes by 3 shuffles.  P.V: thread (group gp, head ph, float4 column
-    // pc) accumulates slots i = gp mod 4; the 4 group sums are added at the end.
+    // 8 lanes by 3 shuffles.  P.V: warp gp accumulates slots i = gp mod 8 for
+    // both heads (lane pc: float4 column pc), so each V row is read once; the
+    // 8 warps' sums are added in warp order at the end.
     const int sg = lane >> 3, st8 = lane & 7;
     float4 qa[2][4];
 #pragma unroll
@@ -192,8 +193,8 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             qa[h][j] = reinterpret_cast<const float4*>(sm.q[h < n_rep ? h : 0])[st8 + 8 * j];
-    const int pc = tid & 31, ph = (tid >> 5) & 1, gp = tid >> 6;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int pc = lane, gp = warp;
+    float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     uint32_t phase = 0;
     for (int rd = 0; rd < n_rounds; ++rd) {
@@ -269,30 +270,37 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             l_run[h] = l_run[h] * corr[h] + (h < n_rep ? sm.lr[h] : 0.f);
             m_run[h] = mnew;
         }
-        if (ph < n_rep) {
-            const float c = corr[ph];
-            acc = make_float4(acc.x * c, acc.y * c, acc.z * c, acc.w * c);
-            const float* pr = sm.p[ph];
-            for (int i = gp; i < ns; i += 4) {
-                const float pi = pr[i];
+        {
+            const float c0 = corr[0], c1 = corr[1];
+            acc0 = make_float4(acc0.x * c0, acc0.y * c0, acc0.z * c0, acc0.w * c0);
+            acc1 = make_float4(acc1.x * c1, acc1.y * c1, acc1.z * c1, acc1.w * c1);
+            for (int i = gp; i < ns; i += 8) {
+                const float p0 = sm.p[0][i];
+                const float p1 = n_rep > 1 ? sm.p[1][i] : 0.f;
                 const float4 vv = reinterpret_cast<const float4*>(i < nc ? sm.v[i < nc ? i : 0] : sm.vn)[pc];
-                acc.x = fmaf(pi, vv.x, acc.x);
-                acc.y = fmaf(pi, vv.y, acc.y);
-                acc.z = fmaf(pi, vv.z, acc.z);
-                acc.w = fmaf(pi, vv.w, acc.w);
+                acc0.x = fmaf(p0, vv.x, acc0.x);
+                acc0.y = fmaf(p0, vv.y, acc0.y);
+                acc0.z = fmaf(p0, vv.z, acc0.z);
+                acc0.w = fmaf(p0, vv.w, acc0.w);
+                acc1.x = fmaf(p1, vv.x, acc1.x);
+                acc1.y = fmaf(p1, vv.y, acc1.y);
+                acc1.z = fmaf(p1, vv.z, acc1.z);
+                acc1.w = fmaf(p1, vv.w, acc1.w);
             }
         }
         __syncthreads();  // sm.k / sm.v / sm.p are refilled by the next round
     }
-    // the 4 slot groups' sums, added in group order (K buffer as scratch)
-    float* gsum = &sm.k[0][0];  // [4][2][128]
-    if (ph < n_rep) reinterpret_cast<float4*>(gsum + (gp * 2 + ph) * 128)[pc] = acc;
+    // the 8 warps' sums, added in warp order (K buffer as scratch)
+    float* gsum = &sm.k[0][0];  // [8][2][128]
+    reinterpret_cast<float4*>(gsum + (gp * 2 + 0) * 128)[pc] = acc0;
+    reinterpret_cast<float4*>(gsum + (gp * 2 + 1) * 128)[pc] = acc1;
     __syncthreads();
     const int hh = tid >> 7, d = tid & 127;  // merge: thread (head hh, dim d)
     float o_run = 0.f;
-    if (hh < n_rep)
-        o_run = ((gsum[(0 * 2 + hh) * 128 + d] + gsum[(1 * 2 + hh) * 128 + d]) + gsum[(2 * 2 + hh) * 128 + d]) +
-                gsum[(3 * 2 + hh) * 128 + d];
+    if (hh < n_rep) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) o_run += gsum[(w * 2 + hh) * 128 + d];
+    }
     tl[4] = a.ts ? globaltimer_ns() : 0;
 
     // ---- merge: once every CTA of the cluster is done with its K/V buffers

@@ -291,12 +291,14 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
     // slot's empty barrier, so no warp can wait on a slot's phase r+1 before
     // it has seen phase r complete (mbarrier parity would alias them).
     bool ok = true;
+    unsigned long long t_first = 0;  // debug: first chunk ready in this CTA
     for (int c = 0; c < nch; ++c) {
         const int s = c % S;
         if (!mbar_wait(&hd.full[s], (uint32_t)(c / S) & 1u, a.err)) {
             ok = false;
             break;
         }
+        if (c == 0 && a.ts) t_first = globaltimer_ns();
         const float* slot = ring + (size_t)s * (RG_SLOT / 4);
         const int jb = c * upc, je = min(jb + upc, u1 - u0);
         for (int j = jb + ((warp - jb) % RG_CWARPS + RG_CWARPS) % RG_CWARPS; j < je; j += RG_CWARPS) {
@@ -351,8 +353,13 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
         if (lane == 0) mbar_arrive(&hd.empty[s]);
     }
     if (a.ts) {
+        const unsigned long long t_done = globaltimer_ns();  // this warp's units are stored
         named_sync_consumers();
-        if (tid == 0) stamp_max(a.ts + 3);
+        if (tid == 0) {
+            stamp_max(a.ts + 3);
+            atomicMax(a.ts + 5, t_first);
+        }
+        if (lane == 0) atomicMax(a.ts + 6, t_done);
     }
     if (!ok && lane == 0) {
         // a copy never arrived: let the producer stop, then wait (bounded) for

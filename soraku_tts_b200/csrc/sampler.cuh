@@ -20,10 +20,12 @@
 // identical to the C restatement in the oracle for the same logits and u.
 //
 // Top-k selection: one 2048-bin histogram pass over the top 11 bits of an
-// order-preserving integer key of f finds the bin holding the k-th largest;
-// every element at or above that bin is compacted (typically ~k + a few
-// dozen) and rank-sorted exactly by (key, index).  With top-k off every
-// element is a candidate (slow path, O(V^2 / 256) compares).
+// order-preserving integer key of the merged logit m finds the bin holding
+// the k-th largest m (f = m / T is non-decreasing in m, so the top-k by f
+// lies at or above it); every element at or above the bin below that one is
+// divided by T, compacted (typically ~k + a few dozen) and rank-sorted
+// exactly by (key of f, index).  With top-k off every element is a candidate
+// (slow path, O(V^2 / 256) compares).
 #pragma once
 
 #include "common.cuh"
@@ -189,8 +191,7 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         float m = cv[k];
         if (J.uncond != nullptr) m = __fadd_rn(uv[k], __fmul_rn(J.cfg_scale, __fsub_rn(cv[k], uv[k])));
         if (i == J.bos || i == J.pad || (J.mask_eos && i == J.eos) || i >= V) m = -INFINITY;
-        if (!greedy) m = __fadd_rn(__fdiv_rn(m, J.temperature), 0.0f);
-        fv[k] = m;
+        fv[k] = m;  // merged logit; divided by the temperature once it is a candidate
     }
 
     if (tid == 0 && J.ts) stamp_max(J.ts + 6);
@@ -250,6 +251,10 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         for (int k = 0; k < NPT; ++k)
             if (tid + k * SAMPLER_THREADS < V) atomicAdd(&hist[ord_key(fv[k]) >> 21], 1u);
         Sync::sync();
+        // (the histogram is over the merged logits m: f = m / T + 0 is
+        // non-decreasing in m for T > 0, so the top-k by f lies in the bins
+        // of m at or above the k-th largest m's bin -- up to a rounding tie
+        // at the bin's lower edge, checked after the sort)
         // thread t owns descending bins 2047-8t .. 2040-8t
         int s = 0;
 #pragma unroll
@@ -273,31 +278,61 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         low_key = (uint32_t)sc[9] << 21;
     }
     if (tid == 0 && J.ts) stamp_max(J.ts + 7);
-    // compaction of every element at or above the cutoff bin: slots come from a
-    // block scan of per-thread counts (the rank sort below fixes the order)
-    int mine = 0;
+    // compaction of every element at or above the cutoff bin (f = m / T is
+    // formed only for these): slots come from a block scan of per-thread
+    // counts, the exact rank sort by (key of f, -index) fixes the order.  If
+    // the largest float below the bin, divided by T, could still reach the
+    // k-th largest f (a rounding tie at the bin edge), the bin below is added
+    // and the step repeats, so the top-k set is exact.
+    int C = 0;
+    for (int pass = 0; pass < 3; ++pass) {
+        int mine = 0;
 #pragma unroll
-    for (int k = 0; k < NPT; ++k)
-        mine += (tid + k * SAMPLER_THREADS < V && ord_key(fv[k]) >= low_key) ? 1 : 0;
-    int C;
-    int slot = block_exclusive_scan<Sync>(mine, sc, &C);
+        for (int k = 0; k < NPT; ++k)
+            mine += (tid + k * SAMPLER_THREADS < V && ord_key(fv[k]) >= low_key) ? 1 : 0;
+        int slot = block_exclusive_scan<Sync>(mine, sc, &C);
+        // (m, index) first; the divisions then run one per thread, not once
+        // per loop slot in every warp that holds a candidate there
 #pragma unroll
-    for (int k = 0; k < NPT; ++k) {
-        const int i = tid + k * SAMPLER_THREADS;
-        const uint32_t key = ord_key(fv[k]);
-        if (i < V && key >= low_key)
-            cand[slot++] = ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-    }
-    Sync::sync();
-    // exact rank sort, descending by (key, -index)
-    for (int i = tid; i < C; i += SAMPLER_THREADS) {
-        const unsigned long long ki = cand[i];
-        int rank = 0;
+        for (int k = 0; k < NPT; ++k) {
+            const int i = tid + k * SAMPLER_THREADS;
+            if (i < V && ord_key(fv[k]) >= low_key)
+                cand[slot++] = ((unsigned long long)__float_as_uint(fv[k]) << 32) |
+                               (unsigned long long)(0xffffffffu - (uint32_t)i);
+        }
+        Sync::sync();
+        for (int j = tid; j < C; j += SAMPLER_THREADS) {
+            const unsigned long long c = cand[j];
+            const float f = __fadd_rn(__fdiv_rn(__uint_as_float((uint32_t)(c >> 32)), J.temperature), 0.0f);
+            cand[j] = ((unsigned long long)ord_key(f) << 32) | (c & 0xffffffffull);  // +0.0 folds -0 into +0
+        }
+        Sync::sync();
+        // exact rank sort, descending by (key, -index)
+        if (C & 1) {
+            if (tid == 0) cand[C] = 0ull;  // pad to pairs: key 0 ranks below every candidate
+            Sync::sync();
+        }
+        for (int i = tid; i < C; i += SAMPLER_THREADS) {
+            const unsigned long long ki = cand[i];
+            const ulonglong2* c2 = reinterpret_cast<const ulonglong2*>(cand);
+            int rank = 0;
 #pragma unroll 4
-        for (int j = 0; j < C; ++j) rank += (cand[j] > ki) ? 1 : 0;
-        sorted[rank] = ki;
+            for (int j = 0; j < (C + 1) / 2; ++j) {
+                const ulonglong2 p = c2[j];
+                rank += (p.x > ki) ? 1 : 0;
+                rank += (p.y > ki) ? 1 : 0;
+            }
+            sorted[rank] = ki;
+        }
+        Sync::sync();
+        if (!topk_on || low_key == 0) break;
+        const float below = key_float(low_key - 1u);  // largest value below the bin
+        const float bound = __fadd_rn(__fdiv_rn(below, J.temperature), 0.0f);
+        const float cutoff = key_float((uint32_t)(sorted[J.top_k - 1] >> 32));
+        if (bound < cutoff) break;  // no element below the bin can tie or pass the cutoff
+        // one bin lower (quarter of an octave); a third pass takes every element
+        low_key = (pass == 0 && low_key >= (1u << 21)) ? low_key - (1u << 21) : 0u;
     }
-    Sync::sync();
     if (tid == 0 && J.ts) stamp_max(J.ts + 8);
     // top-k: keep the sorted prefix with f >= cutoff (ties kept); its end is the
     // one position where f >= cutoff is followed by f < cutoff (or the end)
@@ -316,29 +351,41 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         const uint32_t idx = 0xffffffffu - (uint32_t)(sorted[tid] & 0xffffffffull);
         bulk_prefetch_l2(J.pf_rows + (size_t)idx * J.row_floats, (unsigned)J.row_floats * 4u);
     }
+    // e_j, zero-padded to a multiple of 32 (adding +0 to a running sum of
+    // non-negative terms changes nothing, so the sequential passes below run
+    // whole 32-element chunks without per-element tests)
+    const int npad = (n + 31) & ~31;
     const float top = key_float((uint32_t)(sorted[0] >> 32));
-    for (int j = tid; j < n; j += SAMPLER_THREADS)
-        e[j] = skb_exp(__fsub_rn(key_float((uint32_t)(sorted[j] >> 32)), top));
+    for (int j = tid; j < npad; j += SAMPLER_THREADS)
+        e[j] = j < n ? skb_exp(__fsub_rn(key_float((uint32_t)(sorted[j] >> 32)), top)) : 0.0f;
     Sync::sync();
     if (tid == 0 && J.ts) stamp_max(J.ts + 9);
     // Sequential FP32 sums in candidate order, as the oracle does.  One pass
     // (thread 0) forms the running sums P_j = e_0 + ... + e_j in order: the
     // oracle's S1 is P_{n-1}, its S2 is P_{keep-1} and its draw compares the
-    // same running sums, so those need no pass of their own.
-    float* P = e + VMAX;  // running sums, then (top-p) e_j / S1 after them
+    // same running sums, so those need no pass of their own.  Each chunk's 32
+    // terms are loaded first, then added as one dependent chain.
+    float* P = e + VMAX;  // running sums
     if (tid == 0) {
         float run = 0.0f;
-        for (int j0 = 0; j0 < n; j0 += 8) {
-            float v[8];
+        for (int j0 = 0; j0 < npad; j0 += 32) {
+            float v[32];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? e[j0 + t] : 0.f;
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                if (j0 + t < n) {
-                    run = __fadd_rn(run, v[t]);
-                    P[j0 + t] = run;
-                }
+            for (int t = 0; t < 32; t += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(e + j0 + t);
+                v[t] = q.x;
+                v[t + 1] = q.y;
+                v[t + 2] = q.z;
+                v[t + 3] = q.w;
             }
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+                run = __fadd_rn(run, v[t]);
+                v[t] = run;
+            }
+#pragma unroll
+            for (int t = 0; t < 32; t += 4)
+                *reinterpret_cast<float4*>(P + j0 + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
         }
         sc[11] = n;
     }
@@ -346,25 +393,36 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
     const bool topp_on = J.top_p > 0.0f && J.top_p < 1.0f;
     if (topp_on) {
         const float s1 = P[n - 1];
-        // e_j / S1 in parallel, then its sequential running sum (thread 0);
-        // the prefix is kept up to and including the first j with cum > p
+        // e_j / S1 in parallel (zero-padded), then its sequential running sum
+        // (thread 0); the prefix is kept up to and including the first j with
+        // cum > p
         float* pj = reinterpret_cast<float*>(smem + (size_t)VMAX * 16 + SAMPLER_BINS * 4 + 256);
-        for (int j = tid; j < n; j += SAMPLER_THREADS) pj[j] = __fdiv_rn(e[j], s1);
+        for (int j = tid; j < npad; j += SAMPLER_THREADS) pj[j] = j < n ? __fdiv_rn(e[j], s1) : 0.0f;
         Sync::sync();
         if (tid == 0) {
             int keep = n;
             float cum = 0.0f;
-            for (int j0 = 0; j0 < n && keep == n; j0 += 8) {
-                float v[8];
+            for (int j0 = 0; j0 < npad && keep == n; j0 += 32) {
+                float v[32];
 #pragma unroll
-                for (int t = 0; t < 8; ++t) v[t] = (j0 + t < n) ? pj[j0 + t] : 0.f;
-#pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    if (j0 + t < n && keep == n) {
-                        cum = __fadd_rn(cum, v[t]);
-                        if (cum > J.top_p) keep = j0 + t + 1;
-                    }
+                for (int t = 0; t < 32; t += 4) {
+                    const float4 q = *reinterpret_cast<const float4*>(pj + j0 + t);
+                    v[t] = q.x;
+                    v[t + 1] = q.y;
+                    v[t + 2] = q.z;
+                    v[t + 3] = q.w;
                 }
+#pragma unroll
+                for (int t = 0; t < 32; ++t) {
+                    cum = __fadd_rn(cum, v[t]);
+                    v[t] = cum;
+                }
+                // cum is non-decreasing: the first crossing is the number of
+                // chunk entries not above p
+                int below = 0;
+#pragma unroll
+                for (int t = 0; t < 32; ++t) below += (v[t] > J.top_p) ? 0 : 1;
+                if (below < 32 && j0 + below < n) keep = j0 + below + 1;
             }
             sc[11] = keep;
         }

@@ -159,3 +159,37 @@ def test_fused_sampler_rejects_bad_arguments(lib):
     params = kernels.pack_sample_params([dict(temperature=1.0)])
     with pytest.raises(ValueError):
         kernels.cfg_sample(lg, params, rows_per_req=2, bos_id=BOS, pad_id=PAD, eos_id=EOS)
+
+
+def _bin_edge_tie_case():
+    """top-k whose k-th largest logit sits on a lower edge of the sampler's
+    histogram bins (1.0) with ten logits one float below it: at this
+    temperature those ten divide to the same f as the cutoff, so the top-k
+    set (ties kept) holds 15 entries, 10 of them from the bin below."""
+    t = np.float32(0.30051)
+    edge = np.float32(1.0)
+    below = np.nextafter(edge, np.float32(0))
+    assert np.float32(edge / t) == np.float32(below / t)
+    g = np.random.default_rng(11)
+    cond = (g.standard_normal(V) * 0.2 - 3.0).astype(np.float32)
+    idx = g.permutation(np.arange(10, V - 10))[:15]
+    cond[idx[:4]] = np.array([1.2, 1.15, 1.1, 1.05], np.float32)
+    cond[idx[4]] = edge
+    cond[idx[5:]] = below
+    return cond, float(t)
+
+
+def test_topk_tie_at_histogram_bin_edge():
+    cond, t = _bin_edge_tie_case()
+    _, info = osamp.sample(cond, None, cfg=1.0, temperature=t, top_k=5, top_p=None, mask_eos=True, bos=BOS,
+                           pad=PAD, eos=EOS, u=0.5, return_info=True)
+    assert info["n_kept"] == 15  # the oracle keeps the ties below the bin edge
+    cases = [dict(cond=cond, uncond=None, cfg=1.0, temperature=t, top_k=5, top_p=None, mask_eos=True, seed=s,
+                  request=0, frame=0, q=0) for s in range(48)]
+    codes, _ = _run_cases(cases)
+    picked_below = 0
+    for c, code in zip(cases, codes):
+        want = _oracle(c, osamp.uniform(c["seed"], 0, 0, 0))
+        assert code == want
+        picked_below += cond[code] < 1.0
+    assert picked_below > 0  # the draw reached the tied entries
