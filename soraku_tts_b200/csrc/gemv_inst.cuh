@@ -16,9 +16,19 @@ namespace skb {
 template <int KQ, int XMV, int EMV>
 static cudaError_t gemv_go(const GemvArgs& a, const RgPlan& p, cudaStream_t s, bool pdl) {
     constexpr bool XR = (KQ == 8 && GEMV_M <= 2);
-    auto kern = rgemv_kernel<GEMV_M, KQ, XMV, EMV, XR>;
-    if (p.grid <= 0)  // prepare only
-        return set_smem_attrs(kern, RG_SMEM_MAX);
+    constexpr bool KS_OK = (KQ > 8 && EMV != E_SWIGLU && GEMV_M * RG_KS_UNITS <= 32);
+    auto kern = rgemv_kernel<GEMV_M, KQ, XMV, EMV, XR, false>;
+    if constexpr (KS_OK) {
+        auto kks = rgemv_kernel<GEMV_M, KQ, XMV, EMV, false, true>;
+        if (p.grid <= 0) {  // prepare only
+            const cudaError_t e = set_smem_attrs(kks, RG_SMEM_MAX);
+            if (e != cudaSuccess) return e;
+        } else if (p.ks) {
+            return launch(kks, dim3(p.grid), dim3(RG_THREADS), p.smem, s, pdl, a, p.slots);
+        }
+    }
+    if (p.grid <= 0) return set_smem_attrs(kern, RG_SMEM_MAX);
+    if (p.ks) return cudaErrorInvalidValue;
     return launch(kern, dim3(p.grid), dim3(RG_THREADS), p.smem, s, pdl, a, p.slots);
 }
 

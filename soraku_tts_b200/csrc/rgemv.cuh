@@ -91,17 +91,27 @@ __device__ __forceinline__ void rg_issue(const GemvArgs& a, bool swiglu, int upc
     }
 }
 
+// Units per CTA the K-split mode holds in registers.
+constexpr int RG_KS_UNITS = 8;
+
 // KQ: float4 columns per lane (K <= 128 * KQ).  XR: activations in registers.
+// KS (K-split, for K > 1024 without SwiGLU, at most RG_KS_UNITS units per
+// CTA): warp w takes float4 columns lane + 32q, q = w, w+8, ..., of every
+// unit -- the same columns its prologue normalised, so the activations stay
+// in its registers and no warp reads them from shared memory -- and the 8
+// warps' partial sums meet in shared memory once, after the last chunk.
 // rsm: the kernel's dynamic shared memory.  Returns false in the producer
 // warp (which is done once it has issued every copy), true in the consumer
 // warps once this CTA's outputs are stored.
-template <int M, int KQ, int XM, int EM, bool XR>
+template <int M, int KQ, int XM, int EM, bool XR, bool KS>
 __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, unsigned char* rsm) {
     constexpr bool SW = (EM == E_SWIGLU);
+    static_assert(!KS || (!SW && !XR && M * RG_KS_UNITS <= 32), "K-split: no SwiGLU, <= 32 partial sums");
     constexpr int KP4 = KQ * 32;  // padded float4 columns per activation row
+    constexpr size_t XB = KS ? 0 : (size_t)M * KP4 * 16;  // staged activations
     RgHead& hd = *reinterpret_cast<RgHead*>(rsm);
-    float4* xs = reinterpret_cast<float4*>(rsm + RG_HEAD);  // [M][KP4]
-    float* ring = reinterpret_cast<float*>(rsm + RG_HEAD + (size_t)M * KP4 * 16);
+    float4* xs = reinterpret_cast<float4*>(rsm + RG_HEAD);  // [M][KP4] (not with KS)
+    float* ring = reinterpret_cast<float*>(rsm + RG_HEAD + XB);
     __shared__ float red[2][RG_CWARPS][M];
     __shared__ float epi[RG_EPI_MAX];  // this CTA's residuals or bias values
 
@@ -264,7 +274,7 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
         for (int qi = 0; qi < QW; ++qi) {
             const int q = warp + RG_CWARPS * qi, c4 = lane + 32 * q;
             if (q < KQ) {
-                xs[m * KP4 + c4] = xo[m][qi];
+                if (!KS) xs[m * KP4 + c4] = xo[m][qi];
                 if (NORM && a.xout != nullptr && blockIdx.x == 0 && c4 < K4)
                     reinterpret_cast<float4*>(a.xout + (size_t)m * a.K)[c4] = xo[m][qi];
             }
@@ -283,6 +293,67 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
             for (int q = 0; q < KQ; ++q) xv[XR ? m : 0][XR ? q : 0] = xs[m * KP4 + lane + 32 * q];
     }
 
+    bool ok = true;
+    unsigned long long t_first = 0, t_last = 0;  // debug: first / last chunk ready in this CTA
+    if constexpr (KS) {
+        // ------------------------------------------- units, K split over warps
+        constexpr int NVK = RG_KS_UNITS * M;  // (unit, row) partial sums per lane
+        constexpr int SHK = 5 - Log2<NVK>::value;
+        __shared__ float kpart[RG_CWARPS][NVK];
+        float acc[NVK];
+#pragma unroll
+        for (int v = 0; v < NVK; ++v) acc[v] = 0.f;
+        for (int c = 0; c < nch; ++c) {
+            const int s = c % S;
+            if (!mbar_wait(&hd.full[s], (uint32_t)(c / S) & 1u, a.err)) {
+                ok = false;
+                break;
+            }
+            if (c == 0 && a.ts) t_first = globaltimer_ns();
+            if (c == nch - 1 && a.ts) t_last = globaltimer_ns();
+            const float* slot = ring + (size_t)s * (RG_SLOT / 4);
+            const int jb = c * upc;
+#pragma unroll
+            for (int jj = 0; jj < RG_KS_UNITS; ++jj) {
+                // unit jj of this CTA, when it lies in chunk c
+                if (jj >= jb && jj < jb + upc && jj < nunits) {
+                    const float4* w = reinterpret_cast<const float4*>(slot + (size_t)(jj - jb) * a.K);
+#pragma unroll
+                    for (int qi = 0; qi < QW; ++qi) {
+                        const int c4 = lane + 32 * (warp + RG_CWARPS * qi);
+                        if (warp + RG_CWARPS * qi < KQ && c4 < K4) {
+                            const float4 wv = w[c4];
+#pragma unroll
+                            for (int m = 0; m < M; ++m) {
+                                float t = acc[jj * M + m];
+                                t = fmaf(wv.x, xo[m][qi].x, t);
+                                t = fmaf(wv.y, xo[m][qi].y, t);
+                                t = fmaf(wv.z, xo[m][qi].z, t);
+                                t = fmaf(wv.w, xo[m][qi].w, t);
+                                acc[jj * M + m] = t;
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&hd.empty[s]);
+        }
+        // warp totals of every (unit, row), then the sum over warps in warp order
+        const float res = butterfly_reduce<NVK>(acc, lane);
+        if ((lane & ((1 << SHK) - 1)) == 0) kpart[warp][lane >> SHK] = res;
+        named_sync_consumers();
+        if (tid < nunits * M) {
+            const int j = tid / M, m = tid - j * M;
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < RG_CWARPS; ++w) v += kpart[w][j * M + m];
+            const int n = u0 + j;
+            if (EM == E_RESID) v += stage_epi ? epi[m * nunits + j] : __ldcg(a.resid + (size_t)m * a.ldr + n);
+            if (EM == E_BIAS) v += stage_epi ? epi[j] : __ldg(a.bias + n);
+            a.out[(size_t)m * a.ldo + n] = v;
+        }
+    } else {
     // ------------------------------------------------------------ units
     constexpr int NVR = SW ? 2 * M : M;
     constexpr int NV = NVR <= 1 ? 1 : (NVR <= 2 ? 2 : (NVR <= 4 ? 4 : 8));
@@ -290,8 +361,6 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
     // Every consumer warp visits every chunk in order and arrives once on its
     // slot's empty barrier, so no warp can wait on a slot's phase r+1 before
     // it has seen phase r complete (mbarrier parity would alias them).
-    bool ok = true;
-    unsigned long long t_first = 0;  // debug: first chunk ready in this CTA
     for (int c = 0; c < nch; ++c) {
         const int s = c % S;
         if (!mbar_wait(&hd.full[s], (uint32_t)(c / S) & 1u, a.err)) {
@@ -299,6 +368,7 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
             break;
         }
         if (c == 0 && a.ts) t_first = globaltimer_ns();
+        if (c == nch - 1 && a.ts) t_last = globaltimer_ns();
         const float* slot = ring + (size_t)s * (RG_SLOT / 4);
         const int jb = c * upc, je = min(jb + upc, u1 - u0);
         for (int j = jb + ((warp - jb) % RG_CWARPS + RG_CWARPS) % RG_CWARPS; j < je; j += RG_CWARPS) {
@@ -352,12 +422,14 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
         __syncwarp();
         if (lane == 0) mbar_arrive(&hd.empty[s]);
     }
+    }
     if (a.ts) {
         const unsigned long long t_done = globaltimer_ns();  // this warp's units are stored
         named_sync_consumers();
         if (tid == 0) {
             stamp_max(a.ts + 3);
             atomicMax(a.ts + 5, t_first);
+            atomicMax(a.ts + 7, t_last);
         }
         if (lane == 0) atomicMax(a.ts + 6, t_done);
     }
@@ -375,23 +447,16 @@ __device__ __forceinline__ bool rgemv_body(const GemvArgs& a, const int slots, u
     return true;
 }
 
-template <int M, int KQ, int XM, int EM, bool XR>
+template <int M, int KQ, int XM, int EM, bool XR, bool KS>
 __global__ void __maxnreg__(112) rgemv_kernel(const GemvArgs a, const int slots) {
     extern __shared__ __align__(128) unsigned char rsm[];
-    rgemv_body<M, KQ, XM, EM, XR>(a, slots, rsm);
-}
-
-// Offset of the weight ring in the dynamic shared memory (the region a kernel
-// may reuse once every chunk has been consumed).
-template <int M, int KQ>
-__host__ __device__ constexpr size_t rgemv_ring_offset() {
-    return RG_HEAD + (size_t)M * KQ * 128 * 4;
+    rgemv_body<M, KQ, XM, EM, XR, KS>(a, slots, rsm);
 }
 
 // ------------------------------------------------------------------ host
 struct RgPlan {
     int grid = 0, slots = 0, kq = 0;
-    bool xr = false;
+    bool xr = false, ks = false;
     size_t smem = 0;
 };
 
@@ -405,7 +470,10 @@ inline RgPlan rgemv_plan(int N, int K, int M, int EM, int want) {
     if (unit_bytes > RG_SLOT) return p;
     p.kq = K <= 1024 ? 8 : (K <= 2048 ? 16 : 24);
     p.xr = (p.kq == 8 && M <= 2);
-    const size_t xbytes = (size_t)M * p.kq * 128 * 4;
+    const int NU0 = (EM == E_SWIGLU) ? N / 2 : N;
+    const int G0 = want < NU0 ? (want < 1 ? 1 : want) : NU0;
+    p.ks = p.kq > 8 && EM != E_SWIGLU && (NU0 + G0 - 1) / G0 <= RG_KS_UNITS && M * RG_KS_UNITS <= 32;
+    const size_t xbytes = p.ks ? 0 : (size_t)M * p.kq * 128 * 4;
     const size_t budget = p.kq == 24 ? RG_SMEM_BUDGET_K3072 : RG_SMEM_BUDGET;
     const size_t avail = budget > RG_HEAD + xbytes + 2 * RG_SLOT ? budget - RG_HEAD - xbytes : 2 * RG_SLOT;
     p.slots = (int)(avail / RG_SLOT);
