@@ -85,6 +85,8 @@ struct skb_engine {
     cudaGraphExec_t exec = nullptr;
     int graph_active = 0, graph_fpg = 0, graph_pdl = 0;
     int debug = 0;
+    float* xn = nullptr;  // batched path: normalised activations [R][max inner size]
+    int frame_nodes = 0;  // kernels of the last built frame
     unsigned long long* kts = nullptr;  // debug kernel timeline [kernels per frame][SKB_KTS_STRIDE]
     std::vector<int> frames_host, pos_host;
     std::vector<ReqState> st_host;
@@ -339,15 +341,84 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
 
 // Separate kernels: one GEMV launch per GEMV phase (+ the sampler after the
 // classifier), one attention launch per attention phase.
+// Batched rows (more than the ring GEMV's 4): the phase as a row-norm kernel
+// (when its prologue normalises) and a tiled FP32 GEMM over all rows, then
+// the position advance of the frame's last GEMV.
+void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& nodes) {
+    const GemvArgs& g = ph.g;
+    if (ph.xm != X_PLAIN) {
+        NormRowsArgs na = {};
+        na.x = g.x;
+        na.ldx = g.ldx;
+        na.x2 = g.x2;
+        na.ldx2 = g.ldx2;
+        na.x2_div = g.x2_div > 0 ? g.x2_div : 1;
+        na.nw = g.nw;
+        na.eps = g.neps;
+        na.nw2 = g.nw2;
+        na.eps2 = g.neps2;
+        na.xn = e->xn;
+        na.xout = g.xout;
+        na.hout = g.hout;
+        na.D = g.K;
+        na.mode = ph.xm == X_NORM_ADD_NORM ? 3 : 1;
+        Node n;
+        n.ctas = R;
+        n.run = [na, R](cudaStream_t s, bool pdl, const PrefetchList&) {
+            return norm_rows(na, R, s, pdl) == SKB_OK ? cudaSuccess : cudaErrorUnknown;
+        };
+        nodes.push_back(n);
+    }
+    GemmArgs a = {};
+    a.A = ph.xm == X_PLAIN ? g.x : e->xn;
+    a.lda = ph.xm == X_PLAIN ? g.ldx : g.K;
+    a.w0 = g.w0;
+    a.w1 = g.w1;
+    a.w2 = g.w2;
+    a.seg1 = g.seg1;
+    a.seg2 = g.seg2;
+    a.interleave = g.interleave;
+    a.N = g.N;
+    a.K = g.K;
+    a.T = R;
+    a.out = g.out;
+    a.ldo = g.ldo;
+    a.resid = g.resid;
+    a.ldr = g.ldr;
+    a.bias = g.bias;
+    a.mode = ph.em == E_RESID ? 1 : (ph.em == E_BIAS ? 2 : (ph.em == E_SWIGLU ? 3 : 0));
+    Node n;
+    n.w = gemv_ranges(g);
+    n.ctas = ((a.N + 63) / 64) * ((R + 63) / 64);
+    n.run = [a](cudaStream_t s, bool pdl, const PrefetchList&) { return sgemm_launch(a, s, pdl); };
+    nodes.push_back(n);
+    if (g.inc != nullptr) {
+        int* inc = g.inc;
+        const int n_inc = g.n_inc;
+        Node adv;
+        adv.ctas = 1;
+        adv.run = [inc, n_inc](cudaStream_t s, bool pdl, const PrefetchList&) {
+            return advance_launch(inc, n_inc, s, pdl);
+        };
+        nodes.push_back(adv);
+    }
+}
+
 std::vector<Node> build_frame(skb_engine* e, int n_active) {
     const int R = n_active * e->rpr;
     std::vector<Node> nodes;
-    auto stamps = [e, &nodes]() { return e->debug ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr; };
+    // debug timeline: the ring-GEMV frame only (its kernel count is what kts holds)
+    auto stamps = [e, &nodes, R]() {
+        return (e->debug && R <= 4) ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr;
+    };
     for (const Phase& ph : build_phases(e, n_active)) {
         if (ph.kind == PH_GEMV) {
             GemvArgs g = ph.g;
             g.ts = stamps();
-            nodes.push_back(gemv_node(e, g, R, ph.xm, ph.em));
+            if (R > 4)
+                gemm_rows_nodes(e, ph, R, nodes);
+            else
+                nodes.push_back(gemv_node(e, g, R, ph.xm, ph.em));
             if (ph.sample) {
                 DepthSampleArgs a = ph.s;
                 a.ts = stamps();
@@ -377,6 +448,7 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
             nodes.push_back(n);
         }
     }
+    e->frame_nodes = (int)nodes.size();
     return nodes;
 }
 
@@ -454,8 +526,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     if (m.n_codebooks > 32 || m.n_codebooks < 1) return fail(SKB_ERR_ARG, "1..32 codebooks supported");
     if (opts->rows_per_request != 1 && opts->rows_per_request != 2)
         return fail(SKB_ERR_ARG, "rows_per_request must be 1 or 2");
-    if (opts->max_requests < 1 || opts->max_requests * opts->rows_per_request > 4)
-        return fail(SKB_ERR_ARG, "max_requests * rows_per_request must be 1..4 for the decode GEMV");
+    if (opts->max_requests < 1 || opts->max_requests * opts->rows_per_request > 512)
+        return fail(SKB_ERR_ARG, "max_requests * rows_per_request must be 1..512");
     if (opts->max_len < 2 || opts->max_frames < 1 || opts->max_prefill < 1 || opts->max_prefill > opts->max_len)
         return fail(SKB_ERR_ARG, "bad capacities (max_len %d, max_frames %d, max_prefill %d)", opts->max_len,
                     opts->max_frames, opts->max_prefill);
@@ -527,6 +599,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->page_table, (size_t)e->R * e->max_pages)
     A(e->err, 8)
     A(e->kts, (size_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5))
+    if (e->R > 4) A(e->xn, (size_t)e->R * 3072)
     A(e->host_flag, 1)
     A(e->cur_codes, (size_t)e->nreq * e->Q)
     A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
@@ -899,7 +972,7 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
         case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
-        case 8: *ptr = e->kts; *numel = (int64_t)SKB_KTS_STRIDE * skb_engine_kernels_per_frame(e); break;
+        case 8: *ptr = e->kts; *numel = (int64_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5); break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }
     return SKB_OK;
@@ -914,7 +987,7 @@ int skb_engine_set_debug(skb_engine* e, int on) {
 
 int skb_engine_kernels_per_frame(skb_engine* e) {
     if (!e) return -1;
-    return e->Q * 4 + e->L * 5;
+    return e->frame_nodes > 0 ? e->frame_nodes : e->Q * 4 + e->L * 5;
 }
 
 int skb_engine_launches_per_step(skb_engine* e) {

@@ -64,6 +64,79 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
     }
 }
 
+// Row norms of the batched decode path (more rows than the ring GEMV serves),
+// one CTA per row, D <= 3072:
+//   mode 1: xn = rmsnorm(x; nw, eps)
+//   mode 3: h = rmsnorm(x; nw2, eps2) -> hout;  xn = rmsnorm(h + x2[row / x2_div]; nw, eps) -> xout
+// (the same arithmetic as the ring GEMV's X_RMSNORM / X_NORM_ADD_NORM prologues).
+__global__ void __launch_bounds__(256) norm_rows_kernel(const NormRowsArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float red[8];
+    constexpr int PT = 12;  // D / 256
+    const int r = blockIdx.x, tid = threadIdx.x;
+    float v[PT];
+    const float* xr = a.x + (size_t)r * a.ldx;
+#pragma unroll
+    for (int j = 0; j < PT; ++j) {
+        const int i = tid + 256 * j;
+        v[j] = i < a.D ? __ldcg(xr + i) : 0.f;
+    }
+    auto inv_rms = [&](float eps) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < PT; ++j) ss += v[j] * v[j];
+        ss = warp_sum(ss);
+        __syncthreads();
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += red[w];
+        return rsqrtf(t / (float)a.D + eps);
+    };
+    if (a.mode == 3) {
+        const float inv = inv_rms(a.eps2);
+        const float* x2 = a.x2 + (size_t)(r / a.x2_div) * a.ldx2;
+#pragma unroll
+        for (int j = 0; j < PT; ++j) {
+            const int i = tid + 256 * j;
+            if (i < a.D) {
+                const float h = a.nw2[i] * (v[j] * inv);
+                if (a.hout) a.hout[(size_t)r * a.D + i] = h;
+                v[j] = h + __ldcg(x2 + i);
+            }
+        }
+    }
+    const float inv = inv_rms(a.eps);
+#pragma unroll
+    for (int j = 0; j < PT; ++j) {
+        const int i = tid + 256 * j;
+        if (i < a.D) {
+            const float o = a.nw[i] * (v[j] * inv);
+            a.xn[(size_t)r * a.D + i] = o;
+            if (a.xout) a.xout[(size_t)r * a.D + i] = o;
+        }
+    }
+}
+
+int norm_rows(const NormRowsArgs& a, int rows, cudaStream_t s, bool pdl) {
+    if (a.D > 3072 || rows < 1) return fail(SKB_ERR_ARG, "norm_rows: D %d rows %d", a.D, rows);
+    cudaError_t e = launch(norm_rows_kernel, dim3(rows), dim3(256), 0, s, pdl, a);
+    return e == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "norm_rows: %s", cudaGetErrorString(e));
+}
+
+// Adds 1 to cnt[0 .. n).
+__global__ void advance_kernel(int* cnt, int n) {
+    pdl_wait();
+    pdl_trigger();
+    if ((int)threadIdx.x < n) cnt[threadIdx.x] += 1;
+}
+
+cudaError_t advance_launch(int* cnt, int n, cudaStream_t s, bool pdl) {
+    return launch(advance_kernel, dim3(1), dim3(n < 32 ? 32 : ((n + 31) / 32) * 32), 0, s, pdl, cnt, n);
+}
+
 int rmsnorm_rows(const float* x, const float* x2, const float* w, float* out, int B, int D,
                  float eps, cudaStream_t s, bool pdl) {
     if (B <= 0) return SKB_OK;

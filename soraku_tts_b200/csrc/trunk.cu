@@ -177,15 +177,16 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const GemmArgs a) {
                 if (n >= a.N) continue;
                 float v = acc[i][j];
                 if (a.mode == 1) v += a.resid[(size_t)t * a.ldr + n];
+                if (a.mode == 2) v += __ldg(a.bias + n);
                 a.out[(size_t)t * a.ldo + n] = v;
             }
         }
     }
 }
 
-cudaError_t sgemm_launch(const GemmArgs& a, cudaStream_t s) {
+cudaError_t sgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl) {
     if (a.K % 16 != 0) return cudaErrorInvalidValue;
-    return launch(sgemm_kernel, dim3((a.N + 63) / 64, (a.T + 63) / 64), dim3(256), 0, s, false, a);
+    return launch(sgemm_kernel, dim3((a.N + 63) / 64, (a.T + 63) / 64), dim3(256), 0, s, pdl, a);
 }
 
 // Per token: q/k RMSNorm + RoPE at the token's position; q -> Qo, k/v -> KV.

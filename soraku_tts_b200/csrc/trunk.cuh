@@ -70,7 +70,8 @@ struct GemmArgs {
     int ldo;
     const float* resid;
     int ldr;
-    int mode;  // 0 store, 1 resid, 3 swiglu
+    const float* bias;  // [N] (mode 2)
+    int mode;  // 0 store, 1 resid, 2 bias, 3 swiglu
 };
 
 
