@@ -47,6 +47,9 @@ FRAME_RATE = 12.5  # codec frames per second of audio
 WORKLOADS = {
     "config2": dict(n_text=96, n_ref=144, frames=600),
     "config1": dict(n_text=48, n_ref=72, frames=150),
+    # 64 requests with ragged prompts decoded together (128 CFG rows), split
+    # by request over the GPUs
+    "config4": dict(requests=64, frames=250, text=(16, 96), ref=(24, 144)),
 }
 SAMPLING = dict(cfg_scale=1.5, temperature=0.9, top_k=50, top_p=0.95)
 BOS_TEXT = 151643
@@ -412,9 +415,165 @@ def b200_main(args, wl):
     return 0
 
 
+# ------------------------------------------------------------------ config 4
+def config4_requests(n_req: int, text, ref):
+    """Seeded ragged requests: (ids [1, 1+t], uncond [1, 1], prompt [r, 16], seed)."""
+    out = []
+    for i in range(n_req):
+        rng = np.random.default_rng(5000 + i)
+        t = int(rng.integers(text[0], text[1] + 1))
+        r = int(rng.integers(ref[0], ref[1] + 1))
+        ids, uncond, prompt = make_inputs(5000 + i, t, r)
+        out.append((ids, uncond, prompt, 7000 + i))
+    return out
+
+
+def split_requests(reqs, frames: int, world: int):
+    """Static split balanced on (prompt length + frames): longest first, each
+    to the least-loaded rank."""
+    order = sorted(range(len(reqs)), key=lambda i: -(reqs[i][0].shape[1] + reqs[i][2].shape[0] + frames))
+    load = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in order:
+        w = min(range(world), key=lambda k: load[k])
+        parts[w].append(i)
+        load[w] += reqs[i][0].shape[1] + reqs[i][2].shape[0] + frames
+    return [sorted(p) for p in parts]
+
+
+def config4_main(args, wl):
+    """Batched decode (config 4): every rank decodes its share of the 64
+    requests as one batch of 2 rows per request; value = all ranks' frames
+    over the slowest rank's decode time (fixed total work: strong scaling)."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    from soraku_tts_b200.config import ModelDims
+    from soraku_tts_b200.graph_frame import NativeEngine
+    from soraku_tts_b200.model import SorakuModel
+
+    frames = args.frames or wl["frames"]
+    fpg = max(1, min(args.fpg, frames))
+    while frames % fpg:  # a whole number of graph replays per utterance
+        fpg -= 1
+    reqs = config4_requests(wl["requests"], wl["text"], wl["ref"])
+    mine = split_requests(reqs, frames, world)[rank]
+    n = len(mine)
+    dims = ModelDims()
+    model = SorakuModel.random(dims, 42, f"cuda:{local}")
+    max_prompt = max(r[0].shape[1] + r[2].shape[0] + 2 for r in reqs)
+    max_len = ((max_prompt + frames + 2 + 63) // 64) * 64
+    eng = NativeEngine(model, max_requests=n, rows_per_request=2, max_len=max_len, max_frames=frames,
+                       max_prefill=max_prompt + 2, use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def prefill_all(step):
+        for j, i in enumerate(mine):
+            ids, uncond, prompt, seed = reqs[i]
+            eng.set_sampling(j, cfg=SAMPLING["cfg_scale"], temperature=0.9, temperature_q0=0.9, top_k=50,
+                             top_p=0.95, top_k_q0=50, top_p_q0=0.95, seed=seed + 1000 * step,
+                             min_new_frames=frames, eos_rule=1)
+            eng.prefill(j, ids, uncond, prompt)
+
+    prefill_all(0)
+    eng.capture(n, fpg)
+    for w in range(args.warmup):
+        prefill_all(w)
+        for _ in range(frames // fpg):
+            eng.step(True)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    clocks.start()
+    for s_ in range(args.steps):
+        prefill_all(100 + s_)
+        ev[s_][0].record(stream)
+        for _ in range(frames // fpg):
+            eng.step(True)
+        ev[s_][1].record(stream)
+    barrier()
+    clk = clocks.stop()
+    dec_ms = [a.elapsed_time(b) for a, b in ev]
+    dec_s = max_over_ranks(sum(dec_ms) / 1e3)
+    total_frames = wl["requests"] * frames * args.steps
+    value = total_frames / dec_s
+    for j in range(n):
+        c = eng.read_codes(j, 0, frames)
+        assert c.shape == (frames, 16) and int(c.max()) < 2048 and int(c.min()) >= 0
+
+    # end to end: prefill from host ids, decode, codes back to host
+    barrier()
+    t0 = time.perf_counter()
+    h2d = d2h = 0
+    for s_ in range(args.steps):
+        prefill_all(200 + s_)
+        for _ in range(frames // fpg):
+            eng.step(True)
+        for j in range(n):
+            eng.read_codes(j, 0, frames).cpu()
+            d2h += frames * 16 * 8
+    for i in mine:
+        h2d += reqs[i][0].nbytes + reqs[i][1].nbytes + reqs[i][2].nbytes
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    launches = int(eng.launches_per_step() * (frames // fpg) * args.steps)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(statistics.mean(dec_ms), 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {
+            "workload": f"config4: {wl['requests']} requests (text U{list(wl['text'])}, ref U{list(wl['ref'])}), "
+                        f"{frames} frames each, CFG 1.5, T 0.9, top-k 50, top-p 0.95, split by request over the GPUs",
+            "model": "soraku-TTS v2 talker (Qwen3 28L d1024 16/8 heads, FFN 3072) + depth head, random-init seed 42",
+            "global_batch": wl["requests"], "rows_per_gpu": 2 * n, "parallelism": f"requests split over {world}",
+            "frames_per_graph": fpg, "step_ms_per_frame": round(statistics.mean(dec_ms) / frames, 4),
+            "l2": "inputs larger than L2",
+        },
+        "e2e": {"value": round(total_frames / e2e_s, 1), "unit": "frames/s", "h2d_bytes_per_step": h2d // args.steps,
+                "d2h_bytes_per_step": d2h // args.steps},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     wl = WORKLOADS[args.workload]
+    if args.workload == "config4" and args.impl != "reference":
+        return config4_main(args, wl)
     if args.impl == "reference":
         return reference_main(args, wl)
     if args.kernel_only:
