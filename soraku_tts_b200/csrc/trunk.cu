@@ -424,6 +424,25 @@ int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, cons
 
 }  // namespace skb
 
+extern "C" int skb_test_gemm(const float* x, const float* w, float* out, int M, int N, int K, int tensor_cores,
+                             cudaStream_t stream) {
+    using namespace skb;
+    if (!x || !w || !out || M < 1 || N < 1 || K < 32 || K % 32 != 0)
+        return fail(SKB_ERR_ARG, "test_gemm: bad arguments (M=%d N=%d K=%d)", M, N, K);
+    GemmArgs a = {};
+    a.A = x;
+    a.lda = K;
+    a.w0 = w;
+    a.seg1 = a.seg2 = 1 << 30;
+    a.N = N;
+    a.K = K;
+    a.T = M;
+    a.out = out;
+    a.ldo = N;
+    const cudaError_t e = tensor_cores ? tgemm_launch(a, stream, false) : sgemm_launch(a, stream, false);
+    return e == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "test_gemm: %s", cudaGetErrorString(e));
+}
+
 extern "C" int skb_decode_attention(const float* qkv, int rows, int n_heads, int n_kv_heads, int head_dim,
                                     const float* q_norm, const float* k_norm, float eps, const float* rope_cos,
                                     const float* rope_sin, int max_len, const int32_t* pos, float* kv_pool,

@@ -72,6 +72,7 @@ struct GemmArgs {
     int ldr;
     const float* bias;  // [N] (mode 2)
     int mode;  // 0 store, 1 resid, 2 bias, 3 swiglu
+    int* err;  // optional: set when a wait timed out (tensor-core GEMM)
 };
 
 

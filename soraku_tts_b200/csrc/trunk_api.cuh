@@ -18,6 +18,8 @@ cudaError_t prefill_embed_launch(const PrefillTok* toks, int T, const float* emb
 cudaError_t speaker_launch(const float* v, int SD, const float* W, int D, const float* slot,
                            float* out, cudaStream_t s);
 cudaError_t sgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl = false);
+// 3xTF32 tcgen05 GEMM (tgemm.cu); K a multiple of 32.
+cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl = false);
 cudaError_t prefill_qk_launch(const float* qkv, int ld, const PrefillTok* toks, int T,
                               const float* qn, const float* kn, float eps, const float* rc,
                               const float* rs, int H, const KVLayout& kv, int layer, float* Qo,
