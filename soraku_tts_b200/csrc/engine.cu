@@ -342,8 +342,8 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
 // Separate kernels: one GEMV launch per GEMV phase (+ the sampler after the
 // classifier), one attention launch per attention phase.
 // Batched rows (more than the ring GEMV's 4): the phase as a row-norm kernel
-// (when its prologue normalises) and a tiled FP32 GEMM over all rows, then
-// the position advance of the frame's last GEMV.
+// (when its prologue normalises) and the 3xTF32 tensor-core GEMM over all
+// rows, then the position advance of the frame's last GEMV.
 void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& nodes) {
     const GemvArgs& g = ph.g;
     if (ph.xm != X_PLAIN) {
@@ -387,10 +387,11 @@ void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& n
     a.ldr = g.ldr;
     a.bias = g.bias;
     a.mode = ph.em == E_RESID ? 1 : (ph.em == E_BIAS ? 2 : (ph.em == E_SWIGLU ? 3 : 0));
+    a.err = e->err + 2;
     Node n;
     n.w = gemv_ranges(g);
-    n.ctas = ((a.N + 63) / 64) * ((R + 63) / 64);
-    n.run = [a](cudaStream_t s, bool pdl, const PrefetchList&) { return sgemm_launch(a, s, pdl); };
+    n.ctas = ((a.N + 63) / 64) * ((R + 127) / 128);
+    n.run = [a](cudaStream_t s, bool pdl, const PrefetchList&) { return tgemm_launch(a, s, pdl); };
     nodes.push_back(n);
     if (g.inc != nullptr) {
         int* inc = g.inc;
@@ -659,6 +660,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     decode_attn_cluster_prepare();
     trunk_init_attrs();
     gemv_prepare_all();
+    tgemm_prepare();
     const cudaError_t ce = cudaDeviceSynchronize();
     if (ce != cudaSuccess) {
         skb_engine_destroy(e);
@@ -796,7 +798,7 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         g.out = e->pQKV;
         g.ldo = qd + 2 * kvd;
         g.mode = 0;
-        CK(sgemm_launch(g, s));
+        CK(tgemm_launch(g, s));
         CK(prefill_qk_launch(e->pQKV, qd + 2 * kvd, e->ptok, T, LW(e, l, W_QN), LW(e, l, W_KN), m.rms_eps,
                              e->rope_cos, e->rope_sin, e->H, kv, l, e->pQ, s));
         CK(prefill_attn_launch(e->pQ, e->pmeta, e->pmeta + 8, e->pmeta + 16, e->rpr, maxL, e->H, e->n_rep, kv, l,
@@ -814,7 +816,7 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         o.resid = e->pX;
         o.ldr = e->D;
         o.mode = 1;
-        CK(sgemm_launch(o, s));
+        CK(tgemm_launch(o, s));
         stt = rmsnorm_rows(e->pX, nullptr, LW(e, l, W_LN2), e->pN, T, e->D, m.rms_eps, s, false);
         if (stt) return stt;
         GemmArgs gu = {};
@@ -829,7 +831,7 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         gu.out = e->pG;
         gu.ldo = e->F;
         gu.mode = 3;
-        CK(sgemm_launch(gu, s));
+        CK(tgemm_launch(gu, s));
         GemmArgs dn = {};
         dn.A = e->pG;
         dn.lda = e->F;
@@ -843,7 +845,7 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         dn.resid = e->pX;
         dn.ldr = e->D;
         dn.mode = 1;
-        CK(sgemm_launch(dn, s));
+        CK(tgemm_launch(dn, s));
     }
     CK(gather_rows_launch(e->pX, e->pmeta + 24, e->pmeta + 32, e->rpr, e->x, e->D, s));
     // positions, prefix, counters

@@ -425,7 +425,7 @@ int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, cons
 }  // namespace skb
 
 extern "C" int skb_test_gemm(const float* x, const float* w, float* out, int M, int N, int K, int tensor_cores,
-                             cudaStream_t stream) {
+                             int splits, cudaStream_t stream) {
     using namespace skb;
     if (!x || !w || !out || M < 1 || N < 1 || K < 32 || K % 32 != 0)
         return fail(SKB_ERR_ARG, "test_gemm: bad arguments (M=%d N=%d K=%d)", M, N, K);
@@ -439,6 +439,7 @@ extern "C" int skb_test_gemm(const float* x, const float* w, float* out, int M, 
     a.T = M;
     a.out = out;
     a.ldo = N;
+    a.splits = splits;
     const cudaError_t e = tensor_cores ? tgemm_launch(a, stream, false) : sgemm_launch(a, stream, false);
     return e == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "test_gemm: %s", cudaGetErrorString(e));
 }

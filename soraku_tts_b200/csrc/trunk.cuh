@@ -73,6 +73,7 @@ struct GemmArgs {
     const float* bias;  // [N] (mode 2)
     int mode;  // 0 store, 1 resid, 2 bias, 3 swiglu
     int* err;  // optional: set when a wait timed out (tensor-core GEMM)
+    int splits;  // tensor-core GEMM: K splits per output tile (0 = chosen by occupancy)
 };
 
 

@@ -9,6 +9,7 @@ cudaError_t decode_attn_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, b
 // Cluster variant (attn_cluster.cu): a.S = CTAs per (row, kv head), 1..8.
 cudaError_t decode_attn_cluster_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl);
 cudaError_t decode_attn_cluster_prepare();
+cudaError_t tgemm_prepare();
 int decode_attn_cluster_width(int groups);
 cudaError_t prefill_embed_launch(const PrefillTok* toks, int T, const float* embed, int text_vocab,
                                  const float* lang, int n_lang, const int* lang_ids,

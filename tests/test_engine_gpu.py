@@ -110,6 +110,13 @@ def _check_frames(orc, data, meta, codes, logits, *, temperature, top_k, top_p, 
             m_orc = tf["merged"][f, q]
             top_gpu = set(np.argsort(-m_gpu)[:50].tolist())
             top_orc = set(np.argsort(-m_orc)[:50].tolist())
+            if top_gpu != top_orc:
+                # logits within 1e-4 can only swap members tied at the 50th
+                # value (merged = u + 1.5 (c - u) scales the error by <= 2.5)
+                edge = np.sort(m_orc)[-50]
+                swapped = np.array(sorted(top_gpu ^ top_orc))
+                assert np.all(np.abs(m_orc[swapped] - edge) <= 5e-4 * max(1.0, abs(edge))), \
+                    f"frame {f} q {q}: top-50 sets differ beyond a tie at the boundary"
             agree += top_gpu == top_orc
             total += 1
     assert agree / total >= 0.99, f"top-50 agreement {agree}/{total}"
@@ -267,8 +274,9 @@ def test_route_d_slot_and_language_ids(route_d):
 
 
 def test_full_model_config1_prefill_and_decode(full):
-    """28 layers, vocab 151936, config 1's prompt shape (1+48 text ids, 72 frames)."""
+    """28 layers, vocab 151936, config 1's prompt shape (1+48 text ids, 72 frames);
+    16 free-running frames (256 steps) so that the 99% top-50 rate is resolved."""
     data, meta, orc, model = full
-    codes, logits, hidden0 = _decode(model, data, 3, seed=42)
+    codes, logits, hidden0 = _decode(model, data, 16, seed=42)
     assert_close(hidden0, data["hidden"][0], what="full prefill hidden (vs reference golden)", **TOL)
     _check_frames(orc, data, meta, codes, logits, temperature=0.9, top_k=50, top_p=0.95, seed=42)

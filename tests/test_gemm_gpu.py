@@ -1,6 +1,8 @@
 """The batched / prefill GEMM (out = x @ w^T, FP32 operands) on the GPU
-against a float64 reference: the 3xTF32 tcgen05 kernel and the SIMT FP32
-kernel, at shapes with partial row and column tiles.  Tolerance: rel/abs
+against a float64 reference: the 3xTF32 tcgen05 kernel (K splits chosen by
+occupancy, none, 3 and 8 per tile: a cluster reduction in distributed shared
+memory) and the SIMT FP32 kernel, at shapes with partial row and column
+tiles and fewer K stages than splits.  Tolerance: rel/abs
 1e-5 relative to the row scale (3xTF32 keeps ~21 mantissa bits per product)."""
 
 from __future__ import annotations
@@ -19,16 +21,17 @@ def lib():
     return _lib
 
 
-@pytest.mark.parametrize("tensor_cores", [1, 0])
+@pytest.mark.parametrize("tensor_cores,splits", [(1, 0), (1, 1), (1, 3), (1, 8), (0, 0)])
 @pytest.mark.parametrize("M,N,K", [(128, 64, 32), (200, 320, 1024), (7, 1000, 2048), (388, 4096, 1024),
-                                   (128, 1024, 3072)])
-def test_gemm_matches_float64(lib, tensor_cores, M, N, K):
+                                   (128, 1024, 3072), (130, 100, 160)])
+def test_gemm_matches_float64(lib, tensor_cores, splits, M, N, K):
     g = np.random.default_rng(M * 7 + N + K)
     x = g.standard_normal((M, K)).astype(np.float32)
     w = (g.standard_normal((N, K)) * 0.02).astype(np.float32)
     xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
     out = torch.full((M, N), np.nan, dtype=torch.float32, device="cuda")
-    lib.call("skb_test_gemm", xd.data_ptr(), wd.data_ptr(), out.data_ptr(), M, N, K, tensor_cores, lib.stream_ptr())
+    lib.call("skb_test_gemm", xd.data_ptr(), wd.data_ptr(), out.data_ptr(), M, N, K, tensor_cores, splits,
+             lib.stream_ptr())
     got = out.cpu().numpy()
     ref = x.astype(np.float64) @ w.astype(np.float64).T
     scale = np.sqrt((x.astype(np.float64) ** 2).sum(1, keepdims=True) * (w.astype(np.float64) ** 2).sum(1)[None])
