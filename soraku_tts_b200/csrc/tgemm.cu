@@ -12,30 +12,35 @@
 // of `small` leave a relative error around 2^-21 per product: FP32 parity
 // within the 1e-4 tolerance.
 //
-// CTA tile 128 (rows of X) x 64 (rows of W), K in stages of 32, a ring of 4
-// stages.  Every thread copies 6 16-byte chunks of each stage with cp.async
-// (8 threads per 128-byte row segment) straight into the K-major
-// 128-byte-swizzle layout the MMA reads (row r of a tile at (r/8)*1024 +
-// (r%8)*128, its 16-byte chunk c at slot c ^ (r%8)); three stages are in
-// flight while one is multiplied.  When a stage has landed each thread turns
-// its own chunks into the `small` tile (same layout, no barrier needed
-// between copy and split), then one thread issues the stage's 12
-// tcgen05.mma (4 k-steps of 8 x 3 products, M=128, N=64) and commits them to
-// the slot's mbarrier, which frees the slot for the stage 3 ahead.  Weight
-// chunks of the first stages are requested before the wait on the previous
-// kernel (they do not depend on it).
+// CTA tile 128 (rows of X) x 64 (rows of W), K in stages of 32, warp
+// specialised:
+//   warp 0 (one thread)  TMA: 2-D tiled loads (128-byte swizzle, the K-major
+//                        layout the MMA reads) of the X and W boxes of a
+//                        stage into a ring of 6 raw stages; rows past the
+//                        end of X or W arrive as zeros;
+//   warps 2-7            split: `small` of each landed stage into one of two
+//                        small buffers (elementwise, same layout);
+//   warp 1 (one thread)  MMA: 12 tcgen05.mma per stage (4 k-steps of 8 x 3
+//                        products, M=128, N=64) into the TMEM accumulator,
+//                        committed to the stage's raw slot and small buffer.
+// Weight boxes of the first stages are requested before the wait on the
+// previous kernel (they do not depend on it).  For SwiGLU the W tile is 32
+// gate rows then the 32 matching up rows, so accumulator column j pairs with
+// column j + 32.
 //
 // Split-K: grid.z = ks CTAs share an output tile, each over a contiguous
 // range of K stages, launched as one thread-block cluster (1, 1, ks).  Each
 // CTA stages its 128 x 64 accumulator in its own shared memory; after a
 // cluster barrier CTA z sums rows slice z of the tile over the ks CTAs in
 // split order through distributed shared memory (deterministic, no global
-// scratch) and applies the epilogue: store / residual / bias / SwiGLU
-// (interleaved gate, up rows) with coalesced 16-byte stores.
+// scratch) and applies the epilogue (store / residual / bias / SwiGLU) with
+// coalesced 16-byte stores.
 //
 // Descriptor bit layouts (shared-memory matrix descriptor, instruction
 // descriptor) follow the sm_100 UMMA definitions published in CUTLASS/CuTe
 // (cute/arch/mma_sm100_desc.hpp).
+#include <cudaTypedefs.h>
+
 #include "ops.cuh"
 #include "trunk.cuh"
 #include "trunk_api.cuh"
@@ -44,16 +49,24 @@ namespace skb {
 
 constexpr int TG_BM = 128, TG_BN = 64, TG_BK = 32;
 constexpr int TG_THREADS = 256;
-constexpr int TG_A_BYTES = TG_BM * TG_BK * 4;  // 16 KB
-constexpr int TG_B_BYTES = TG_BN * TG_BK * 4;  // 8 KB
-constexpr int TG_RAW = TG_A_BYTES + TG_B_BYTES;  // one stage as copied (read as `big`)
-constexpr int TG_STAGE = 2 * TG_RAW;             // + its `small` parts
-constexpr int TG_STAGES = 4;
+constexpr int TG_A_BYTES = TG_BM * TG_BK * 4;    // 16 KB
+constexpr int TG_B_BYTES = TG_BN * TG_BK * 4;    // 8 KB
+constexpr int TG_RAW = TG_A_BYTES + TG_B_BYTES;  // one stage as loaded (read as `big`)
+constexpr int TG_RS = 6;                         // raw stages in flight
+constexpr int TG_SS = 2;                         // `small` buffers
+constexpr int TG_SPLIT_THREADS = 192;            // warps 2-7
 constexpr int TG_MAX_SPLITS = 8;
 constexpr int TG_OUT_LD = TG_BN + 4;  // staged accumulator row, floats (conflict-free 16-B stores)
-constexpr size_t TG_SMEM = 1024 /* alignment slack */ + (size_t)TG_STAGES * TG_STAGE + 64;
-static_assert(TG_BM * TG_OUT_LD * 4 <= TG_STAGES * TG_STAGE, "staged accumulator fits the ring");
-static_assert(TG_THREADS * 4 == TG_BM * 8 && TG_THREADS * 2 == TG_BN * 8, "6 chunks per thread per stage");
+constexpr int TG_BAR_BYTES = 256;
+constexpr size_t TG_SMEM = 1024 /* alignment slack */ + (size_t)(TG_RS + TG_SS) * TG_RAW + TG_BAR_BYTES;
+static_assert(TG_BM * TG_OUT_LD * 4 <= TG_RS * TG_RAW, "staged accumulator fits the raw ring");
+static_assert((TG_RAW / 16) % TG_SPLIT_THREADS == 0, "split work divides evenly");
+static_assert((2 * TG_RS + 2 * TG_SS + 1) * 8 + 4 <= TG_BAR_BYTES, "barriers fit");
+
+// Operand tensor maps: X, then W as up to three row segments (or gate, up).
+struct TgMaps {
+    CUtensorMap a, w[3];
+};
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     // start address >> 4 [0,14); LBO (16 B units) [16,30) = 1; SBO [32,46) = 1024 B / 16;
@@ -85,19 +98,18 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// 16-byte global -> shared copy; `valid` false writes zeros and reads nothing.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ void tg_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ uint32_t tg_off(int r, int c) {
-    return (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u + (uint32_t)((c ^ (r & 7)) * 16);
+// 2-D tiled TMA load of box (x = K offset, y = row) into this CTA's shared
+// memory, completing on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ float4 tg_small(float4 v) {
@@ -109,18 +121,6 @@ __device__ __forceinline__ float4 tg_small(float4 v) {
     return s;
 }
 
-__device__ __forceinline__ const float* tg_wrow(const GemmArgs& a, int n) {
-    if (a.interleave) return ((n & 1) ? a.w1 : a.w0) + (size_t)(n >> 1) * a.K;
-    if (n < a.seg1) return a.w0 + (size_t)n * a.K;
-    if (n < a.seg2) return a.w1 + (size_t)(n - a.seg1) * a.K;
-    return a.w2 + (size_t)(n - a.seg2) * a.K;
-}
-
-__device__ __forceinline__ uint32_t tg_cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
 __device__ __forceinline__ uint32_t tg_cluster_size() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
@@ -137,13 +137,18 @@ __device__ __forceinline__ float4 tg_ld_peer4(uint32_t local, uint32_t rank) {
     return v;
 }
 
-__global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, const __grid_constant__ TgMaps tm) {
     extern __shared__ unsigned char tg_raw[];
     // 1024-byte aligned stage buffers (the swizzle pattern repeats every 1024 B)
     unsigned char* base = tg_raw + ((1024u - (smem_u32(tg_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(base);
-    uint64_t* mma_bar = reinterpret_cast<uint64_t*>(base + TG_STAGES * TG_STAGE);  // [TG_STAGES]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + TG_STAGES);
+    const uint32_t small0 = sbase + TG_RS * TG_RAW;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + (TG_RS + TG_SS) * TG_RAW);  // TMA landed [RS]
+    uint64_t* empty = full + TG_RS;      // MMAs done with a raw slot [RS]
+    uint64_t* sdone = empty + TG_RS;     // `small` written [SS]
+    uint64_t* sfree = sdone + TG_SS;     // MMAs done with a small buffer [SS]
+    uint64_t* accfull = sfree + TG_SS;   // every MMA done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
     __shared__ int tg_err;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -154,107 +159,118 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a) 
     const int sb = (int)((long long)z * nst / ks), se = (int)((long long)(z + 1) * nst / ks);
     const int nloc = se - sb;
 
+    // W box of a stage: 64 rows of one segment, or 32 gate + 32 up rows
+    const CUtensorMap* wmap0;
+    const CUtensorMap* wmap1 = nullptr;
+    int wy;
+    if (a.interleave) {
+        wmap0 = &tm.w[0];
+        wmap1 = &tm.w[1];
+        wy = n0 >> 1;
+    } else if (n0 < a.seg1) {
+        wmap0 = &tm.w[0];
+        wy = n0;
+    } else if (n0 < a.seg2) {
+        wmap0 = &tm.w[1];
+        wy = n0 - a.seg1;
+    } else {
+        wmap0 = &tm.w[2];
+        wy = n0 - a.seg2;
+    }
+    auto load_w = [&](int st, int slot) {
+        const uint32_t dst = sbase + slot * TG_RAW + TG_A_BYTES;
+        if (wmap1) {
+            tma_load_2d(dst, wmap0, st * TG_BK, wy, &full[slot]);
+            tma_load_2d(dst + TG_B_BYTES / 2, wmap1, st * TG_BK, wy, &full[slot]);
+        } else {
+            tma_load_2d(dst, wmap0, st * TG_BK, wy, &full[slot]);
+        }
+    };
+
     if (tid == 0) {
-        for (int s = 0; s < TG_STAGES; ++s) mbar_init(&mma_bar[s], 1);
+        for (int s = 0; s < TG_RS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < TG_SS; ++s) {
+            mbar_init(&sdone[s], TG_SPLIT_THREADS);
+            mbar_init(&sfree[s], 1);
+        }
+        mbar_init(accfull, 1);
         mbar_fence_init();
         // a split grid must run as one cluster per tile (peer reads below)
         tg_err = (ks > 1 && (int)tg_cluster_size() != ks) ? 1 : 0;
+        // weights of the first stages do not depend on the previous kernel
+        for (int i = 0; i < TG_RS && i < nloc; ++i) {
+            mbar_expect_tx(&full[i], TG_RAW);
+            load_w(sb + i, i);
+        }
     }
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TG_BN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-
-    // This thread's chunks of a stage: A rows (tid + 256 j) / 8, j < 4, and
-    // W rows (tid + 256 j) / 8, j < 2; 16-byte column tid % 8.
-    const int c = tid & 7;
-    auto issue_w = [&](int st, int slot) {
-        const uint32_t dst = sbase + slot * TG_STAGE + TG_A_BYTES;
-        const int k0 = st * TG_BK + 4 * c;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int r = (tid + TG_THREADS * j) >> 3, n = n0 + r;
-            const bool ok = n < a.N;
-            cp_async16(dst + tg_off(r, c), ok ? tg_wrow(a, n) + k0 : a.w0, ok);
-        }
-    };
-    auto issue_a = [&](int st, int slot) {
-        const uint32_t dst = sbase + slot * TG_STAGE;
-        const int k0 = st * TG_BK + 4 * c;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int r = (tid + TG_THREADS * j) >> 3, m = m0 + r;
-            const bool ok = m < a.T;
-            cp_async16(dst + tg_off(r, c), ok ? a.A + (size_t)m * a.lda + k0 : a.A, ok);
-        }
-    };
-    auto split_own = [&](int slot) {
-        unsigned char* raw = base + slot * TG_STAGE;
-        unsigned char* sml = raw + TG_RAW;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t o = tg_off((tid + TG_THREADS * j) >> 3, c);
-            *reinterpret_cast<float4*>(sml + o) = tg_small(*reinterpret_cast<const float4*>(raw + o));
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const uint32_t o = TG_A_BYTES + tg_off((tid + TG_THREADS * j) >> 3, c);
-            *reinterpret_cast<float4*>(sml + o) = tg_small(*reinterpret_cast<const float4*>(raw + o));
-        }
-    };
-
-    // weights of the first stages do not depend on the previous kernel
-    for (int i = 0; i < TG_STAGES - 1 && i < nloc; ++i) issue_w(sb + i, i);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
     pdl_wait();
-    // group i holds stage i's activation chunks (group 0 also the weights above)
-    for (int i = 0; i < TG_STAGES - 1; ++i) {
-        if (i < nloc) issue_a(sb + i, i);
-        cp_async_commit();
-    }
-    pdl_trigger();
-
     int err = 0;
-    for (int i = 0; i < nloc; ++i) {
-        const int slot = i % TG_STAGES;
-        cp_async_wait<TG_STAGES - 2>();  // this thread's chunks of stage i have landed
-        split_own(slot);
-        // generic-proxy shared writes -> visible to the tensor core (async proxy)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t ab = sbase + slot * TG_STAGE, bb = ab + TG_A_BYTES;
-            const uint32_t as_ = ab + TG_RAW, bs = bb + TG_RAW;
-#pragma unroll
-            for (int kk = 0; kk < TG_BK / 8; ++kk) {
-                const uint32_t o = kk * 32;  // 8 TF32 = 32 bytes along K
-                umma_tf32(tmem, umma_desc_sw128(ab + o), umma_desc_sw128(bb + o), i > 0 || kk > 0);
-                umma_tf32(tmem, umma_desc_sw128(ab + o), umma_desc_sw128(bs + o), true);
-                umma_tf32(tmem, umma_desc_sw128(as_ + o), umma_desc_sw128(bb + o), true);
+    if (warp == 0) {
+        if (lane == 0) {  // producer
+            for (int i = 0; i < TG_RS && i < nloc; ++i)
+                tma_load_2d(sbase + i * TG_RAW, &tm.a, (sb + i) * TG_BK, m0, &full[i]);
+            pdl_trigger();
+            for (int i = TG_RS; i < nloc; ++i) {
+                const int s = i % TG_RS;
+                if (!mbar_wait(&empty[s], (uint32_t)((i - TG_RS) / TG_RS) & 1u, a.err)) err = 1;
+                mbar_expect_tx(&full[s], TG_RAW);
+                load_w(sb + i, s);
+                tma_load_2d(sbase + s * TG_RAW, &tm.a, (sb + i) * TG_BK, m0, &full[s]);
             }
-            umma_commit(&mma_bar[slot]);
         }
-        // refill: stage i+3 goes into the slot of stage i-1, once its MMAs are done
-        const int nx = i + TG_STAGES - 1;
-        if (nx < nloc) {
-            const int ns = nx % TG_STAGES;
-            if (i >= 1 && !mbar_wait(&mma_bar[ns], (uint32_t)((i - 1) / TG_STAGES) & 1u, a.err)) err = 1;
-            issue_w(sb + nx, ns);
-            issue_a(sb + nx, ns);
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issue
+            for (int i = 0; i < nloc; ++i) {
+                const int s = i % TG_RS, j = i % TG_SS;
+                if (!mbar_wait(&sdone[j], (uint32_t)(i / TG_SS) & 1u, a.err)) err = 1;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t ab = sbase + s * TG_RAW, bb = ab + TG_A_BYTES;
+                const uint32_t as_ = small0 + j * TG_RAW, bs = as_ + TG_A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < TG_BK / 8; ++kk) {
+                    const uint32_t o = kk * 32;  // 8 TF32 = 32 bytes along K
+                    umma_tf32(tmem, umma_desc_sw128(ab + o), umma_desc_sw128(bb + o), i > 0 || kk > 0);
+                    umma_tf32(tmem, umma_desc_sw128(ab + o), umma_desc_sw128(bs + o), true);
+                    umma_tf32(tmem, umma_desc_sw128(as_ + o), umma_desc_sw128(bb + o), true);
+                }
+                umma_commit(&empty[s]);
+                umma_commit(&sfree[j]);
+            }
+            if (nloc > 0) umma_commit(accfull);
         }
-        cp_async_commit();
+    } else {  // split
+        const int t = tid - 64;
+        for (int i = 0; i < nloc; ++i) {
+            const int s = i % TG_RS, j = i % TG_SS;
+            if (!mbar_wait(&full[s], (uint32_t)(i / TG_RS) & 1u, a.err)) err = 1;
+            if (i >= TG_SS && !mbar_wait(&sfree[j], (uint32_t)((i - TG_SS) / TG_SS) & 1u, a.err)) err = 1;
+            const float4* raw = reinterpret_cast<const float4*>(base + s * TG_RAW);
+            float4* sml = reinterpret_cast<float4*>(base + (TG_RS + j) * TG_RAW);
+#pragma unroll
+            for (int q = 0; q < TG_RAW / 16 / TG_SPLIT_THREADS; ++q)
+                sml[t + TG_SPLIT_THREADS * q] = tg_small(raw[t + TG_SPLIT_THREADS * q]);
+            // generic-proxy shared writes -> visible to the tensor core (async proxy)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tg_arrive(&sdone[j]);
+        }
     }
-    // all MMAs done: the last commit covers every earlier MMA of this thread
-    if (nloc > 0 && !mbar_wait(&mma_bar[(nloc - 1) % TG_STAGES], (uint32_t)((nloc - 1) / TG_STAGES) & 1u, a.err))
-        err = 1;
-    cp_async_wait<0>();
+    __syncwarp();
+    // all MMAs done (so every TMA load was consumed)
+    if (nloc > 0 && !mbar_wait(accfull, 0u, a.err)) err = 1;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
     // accumulator -> shared tile [128][TG_OUT_LD]: warp w reads TMEM lanes
@@ -276,7 +292,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a) 
 #pragma unroll
         for (int j = 0; j < 32; ++j) r32[j] = 0u;  // no K range: a zero partial
     }
-    float* acc_s = reinterpret_cast<float*>(base);  // the ring is idle now
+    float* acc_s = reinterpret_cast<float*>(base);  // the raw ring is idle now
     {
         float* row = acc_s + (32 * rq + lane) * TG_OUT_LD + 32 * ch;
 #pragma unroll
@@ -293,69 +309,101 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a) 
         __syncthreads();
     const bool peers_ok = !split || tg_err == 0;
 
-    // rows slice z of the tile: 16-byte groups [z*2048/ks, (z+1)*2048/ks)
-    constexpr int G4 = TG_BM * TG_BN / 4;
-    const int g_lo = split ? (int)(z * G4 / ks) : 0, g_hi = split ? (int)((z + 1) * G4 / ks) : G4;
+    // 16-byte groups of the output: rows x 16 (rows x 8 for SwiGLU, whose
+    // group c pairs gate columns 4c.. with up columns 32+4c..); CTA z of a
+    // split tile owns groups [z*G/ks, (z+1)*G/ks)
+    const bool glu = a.mode == 3;
+    const int per_row = glu ? 8 : 16;
+    const int G = TG_BM * per_row;
+    const int g_lo = split ? (int)((long long)z * G / ks) : 0;
+    const int g_hi = split ? (int)((long long)(z + 1) * G / ks) : G;
     const bool vec_out = ((a.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0);
     const bool vec_res =
         a.mode != 1 || (((a.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.resid) & 15) == 0));
+    const int ncols = glu ? a.N >> 1 : a.N;  // output columns
+    const int c0 = glu ? n0 >> 1 : n0;
     for (int g = g_lo + tid; g < g_hi; g += TG_THREADS) {
-        const int r = g >> 4, c4 = g & 15;
-        const int m = m0 + r, n = n0 + 4 * c4;
-        const uint32_t la = smem_u32(acc_s + r * TG_OUT_LD + 4 * c4);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int r = g / per_row, c4 = g % per_row;
+        const int m = m0 + r, n = c0 + 4 * c4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = v;
+        const float* src = acc_s + r * TG_OUT_LD + 4 * c4;
         if (!split) {
-            v = *reinterpret_cast<const float4*>(acc_s + r * TG_OUT_LD + 4 * c4);
+            v = *reinterpret_cast<const float4*>(src);
+            if (glu) u = *reinterpret_cast<const float4*>(src + 32);
         } else if (peers_ok) {
+            const uint32_t la = smem_u32(src);
             for (int zz = 0; zz < ks; ++zz) {
                 const float4 p = tg_ld_peer4(la, (uint32_t)zz);
-                v.x += p.x;
-                v.y += p.y;
-                v.z += p.z;
-                v.w += p.w;
+                v.x += p.x, v.y += p.y, v.z += p.z, v.w += p.w;
+                if (glu) {
+                    const float4 q = tg_ld_peer4(la + 128u, (uint32_t)zz);
+                    u.x += q.x, u.y += q.y, u.z += q.z, u.w += q.w;
+                }
             }
         }
         if (m >= a.T || tg_err) continue;
-        float* orow = a.out + (size_t)m * a.ldo;
-        if (a.mode == 3) {  // SwiGLU over (gate, up) column pairs
-            if (n + 1 < a.N) orow[n >> 1] = silu(v.x) * v.y;
-            if (n + 3 < a.N) orow[(n >> 1) + 1] = silu(v.z) * v.w;
-            continue;
-        }
         float e[4] = {v.x, v.y, v.z, v.w};
-        if (n + 3 < a.N && vec_out && vec_res) {
+        if (glu) {
+            e[0] = silu(v.x) * u.x;
+            e[1] = silu(v.y) * u.y;
+            e[2] = silu(v.z) * u.z;
+            e[3] = silu(v.w) * u.w;
+        }
+        float* orow = a.out + (size_t)m * a.ldo;
+        if (n + 3 < ncols && vec_out && vec_res) {
             if (a.mode == 1) {
                 const float4 q = __ldcg(reinterpret_cast<const float4*>(a.resid + (size_t)m * a.ldr + n));
                 e[0] += q.x, e[1] += q.y, e[2] += q.z, e[3] += q.w;
             } else if (a.mode == 2) {
 #pragma unroll
-                for (int t = 0; t < 4; ++t) e[t] += __ldg(a.bias + n + t);
+                for (int k = 0; k < 4; ++k) e[k] += __ldg(a.bias + n + k);
             }
             *reinterpret_cast<float4*>(orow + n) = make_float4(e[0], e[1], e[2], e[3]);
         } else {
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                if (n + t >= a.N) break;
-                float val = e[t];
-                if (a.mode == 1) val += __ldcg(a.resid + (size_t)m * a.ldr + n + t);
-                if (a.mode == 2) val += __ldg(a.bias + n + t);
-                orow[n + t] = val;
+            for (int k = 0; k < 4; ++k) {
+                if (n + k >= ncols) break;
+                float val = e[k];
+                if (a.mode == 1) val += __ldcg(a.resid + (size_t)m * a.ldr + n + k);
+                if (a.mode == 2) val += __ldg(a.bias + n + k);
+                orow[n + k] = val;
             }
         }
     }
-    if (tid == 0 && tg_err && a.err != nullptr) atomicExch(a.err, 1);
+    if (tid == 0) {
+        // no copy may still be landing when the CTA exits (only reachable
+        // after a timed-out wait; these phases are complete otherwise)
+        for (int i = nloc > TG_RS ? nloc - TG_RS : 0; i < nloc; ++i)
+            mbar_wait(&full[i % TG_RS], (uint32_t)(i / TG_RS) & 1u, a.err);
+        if (tg_err && a.err != nullptr) atomicExch(a.err, 1);
+    }
     // peers may still read this CTA's tile
     if (split) asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     // release the accumulator
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0)
+    if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TG_BN) : "memory");
 }
 
 namespace {
 int tg_n_sm = 148;
 int tg_max_clusters[TG_MAX_SPLITS + 1];  // resident clusters of (1, 1, c) CTAs
+PFN_cuTensorMapEncodeTiled_v12000 tg_encode = nullptr;
+
+// 2-D map over rows x inner FP32 values (row stride ld floats), box
+// 32 x box_rows, 128-byte swizzle, zero fill outside.
+bool tg_map(CUtensorMap* m, const float* p, int inner, int rows, int ld, int box_rows) {
+    if (rows <= 0) return true;  // segment not present: never read
+    if ((reinterpret_cast<uintptr_t>(p) & 15) != 0 || (ld & 3) != 0) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)TG_BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return tg_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 }  // namespace
 
 cudaError_t tgemm_prepare() {
@@ -363,6 +411,13 @@ cudaError_t tgemm_prepare() {
     if (done) return cudaSuccess;
     cudaError_t e = set_smem_attrs(tgemm_kernel, TG_SMEM);
     if (e != cudaSuccess) return e;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&tg_encode), cudaEnableDefault,
+                                &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || tg_encode == nullptr) {
+        cudaGetLastError();
+        return cudaErrorNotSupported;
+    }
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&tg_n_sm, cudaDevAttrMultiProcessorCount, dev);
@@ -410,11 +465,28 @@ int tgemm_splits(const GemmArgs& a) {
     return ks < 1 ? 1 : ks;
 }
 
-// K a multiple of 32, 16-byte aligned rows.
+// K a multiple of 32; X, W and the row strides 16-byte aligned; SwiGLU
+// (interleave) needs N a multiple of 64, row segments start at multiples of 64.
 cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl) {
     const cudaError_t pe = tgemm_prepare();
     if (pe != cudaSuccess) return pe;
     if (a.K % TG_BK != 0 || a.K <= 0 || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
+    TgMaps tm;
+    memset(&tm, 0, sizeof tm);
+    bool ok = tg_map(&tm.a, a.A, a.K, a.T, a.lda, TG_BM);
+    if (a.interleave) {
+        ok = ok && a.N % TG_BN == 0 && a.mode == 3;
+        ok = ok && tg_map(&tm.w[0], a.w0, a.K, a.N / 2, a.K, TG_BN / 2);
+        ok = ok && tg_map(&tm.w[1], a.w1, a.K, a.N / 2, a.K, TG_BN / 2);
+    } else {
+        ok = ok && a.mode != 3;
+        const int s1 = a.seg1 < a.N ? a.seg1 : a.N, s2 = a.seg2 < a.N ? a.seg2 : a.N;
+        ok = ok && (s1 == a.N || s1 % TG_BN == 0) && (s2 == a.N || s2 % TG_BN == 0) && s1 <= s2;
+        ok = ok && tg_map(&tm.w[0], a.w0, a.K, s1, a.K, TG_BN);
+        ok = ok && tg_map(&tm.w[1], a.w1, a.K, s2 - s1, a.K, TG_BN);
+        ok = ok && tg_map(&tm.w[2], a.w2, a.K, a.N - s2, a.K, TG_BN);
+    }
+    if (!ok) return cudaErrorInvalidValue;
     const int ks = tgemm_splits(a);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((a.N + TG_BN - 1) / TG_BN, (a.T + TG_BM - 1) / TG_BM, ks);
@@ -435,7 +507,7 @@ cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, tgemm_kernel, a);
+    return cudaLaunchKernelEx(&cfg, tgemm_kernel, a, tm);
 }
 
 }  // namespace skb
