@@ -7,32 +7,41 @@
 // bits cleared (exactly a TF32 value) and small = x - big (exact in FP32);
 // the product is big*big + big*small + small*big, accumulated in FP32 in
 // tensor memory.  A kind::tf32 MMA reads only the TF32 bits of each 32-bit
-// operand, so the raw FP32 tile in shared memory serves as `big` and only
-// `small` is computed.  The dropped small*small term and the TF32 truncation
-// of `small` leave a relative error around 2^-21 per product: FP32 parity
-// within the 1e-4 tolerance.
+// operand, so raw FP32 values serve as `big` and only `small` is computed.
+// The dropped small*small term and the TF32 truncation of `small` leave a
+// relative error around 2^-21 per product: FP32 parity within the 1e-4
+// tolerance.
 //
-// CTA tile 128 (rows of X) x 64 (rows of W), K in stages of 32, warp
-// specialised:
+// A TF32 MMA with M = 128 costs nearly the same time for N = 64 and 128 and
+// only ~1.2x that for N = 256 (measured on B200), so the tile is 128 rows of
+// X x 128 rows of W and the W operand of the main product is the stacked
+// [W_big; W_small] (N = 256): per k-step of 8,
+//   D[:, 0:256)  += X_big   . [W_big; W_small]^T    (N = 256)
+//   D[:, 0:128)  += X_small . W_big^T               (N = 128)
+// and the result is D[:, 0:128) + D[:, 128:256).  K runs in stages of 32,
+// warp specialised:
 //   warp 0 (one thread)  TMA: 2-D tiled loads (128-byte swizzle, the K-major
 //                        layout the MMA reads) of the X and W boxes of a
-//                        stage into a ring of 6 raw stages; rows past the
-//                        end of X or W arrive as zeros;
-//   warps 2-7            split: `small` of each landed stage into one of two
-//                        small buffers (elementwise, same layout);
-//   warp 1 (one thread)  MMA: 12 tcgen05.mma per stage (4 k-steps of 8 x 3
-//                        products, M=128, N=64) into the TMEM accumulator,
-//                        committed to the stage's raw slot and small buffer.
-// Weight boxes of the first stages are requested before the wait on the
-// previous kernel (they do not depend on it).  For SwiGLU the W tile is 32
-// gate rows then the 32 matching up rows, so accumulator column j pairs with
-// column j + 32.
+//                        stage into a ring of 4 stages; rows past the end of
+//                        X or W arrive as zeros;
+//   warps 4-7            X to tensor memory: lane l of warp w moves row
+//                        32*(w%4)+l of the stage (its TMEM lane) as big and
+//                        small TF32 columns, so the MMAs read X from TMEM;
+//   warps 2-3            W split: W_small of the stage, written right after
+//                        W_big in the same 128-byte-swizzle layout;
+//   warp 1 (one thread)  MMA: 8 tcgen05.mma per stage, committed to the
+//                        stage's slot (which frees it for the stage 4 ahead).
+// One lane per warp waits on and arrives at the barriers; the warp
+// synchronises around it.  Weight boxes of the first stages are requested
+// before the wait on the previous kernel (they do not depend on it).  For
+// SwiGLU the W box is 64 gate rows then the 64 matching up rows, so result
+// column j pairs with column j + 64.
 //
 // Split-K: grid.z = ks CTAs share an output tile, each over a contiguous
 // range of K stages, launched as one thread-block cluster (1, 1, ks).  Each
-// CTA stages its 128 x 64 accumulator in its own shared memory; after a
-// cluster barrier CTA z sums rows slice z of the tile over the ks CTAs in
-// split order through distributed shared memory (deterministic, no global
+// CTA stages its 128 x 128 result in its own shared memory; after a cluster
+// barrier CTA z sums rows slice z of the tile over the ks CTAs in split
+// order through distributed shared memory (deterministic, no global
 // scratch) and applies the epilogue (store / residual / bias / SwiGLU) with
 // coalesced 16-byte stores.
 //
@@ -47,21 +56,25 @@
 
 namespace skb {
 
-constexpr int TG_BM = 128, TG_BN = 64, TG_BK = 32;
+constexpr int TG_BM = 128, TG_BN = 128, TG_BK = 32;
 constexpr int TG_THREADS = 256;
-constexpr int TG_A_BYTES = TG_BM * TG_BK * 4;    // 16 KB
-constexpr int TG_B_BYTES = TG_BN * TG_BK * 4;    // 8 KB
-constexpr int TG_RAW = TG_A_BYTES + TG_B_BYTES;  // one stage as loaded (read as `big`)
-constexpr int TG_RS = 6;                         // raw stages in flight
-constexpr int TG_SS = 2;                         // `small` buffers
-constexpr int TG_SPLIT_THREADS = 192;            // warps 2-7
+constexpr int TG_X_BYTES = TG_BM * TG_BK * 4;                 // 16 KB
+constexpr int TG_W_BYTES = TG_BN * TG_BK * 4;                 // 16 KB
+constexpr int TG_STAGE = TG_X_BYTES + 2 * TG_W_BYTES;         // X | W_big | W_small
+constexpr int TG_STAGES = 4;
+constexpr int TG_WSPLIT_THREADS = 64;                         // warps 2-3
+constexpr int TG_READY_WARPS = 6;                             // warps 2-7 arrive per stage
+constexpr uint32_t TG_XCOL = 2 * TG_BN;                       // TMEM: result [0, 256), X buffers after
+constexpr uint32_t TG_TMEM_COLS = 512;
 constexpr int TG_MAX_SPLITS = 8;
-constexpr int TG_OUT_LD = TG_BN + 4;  // staged accumulator row, floats (conflict-free 16-B stores)
-constexpr int TG_BAR_BYTES = 256;
-constexpr size_t TG_SMEM = 1024 /* alignment slack */ + (size_t)(TG_RS + TG_SS) * TG_RAW + TG_BAR_BYTES;
-static_assert(TG_BM * TG_OUT_LD * 4 <= TG_RS * TG_RAW, "staged accumulator fits the raw ring");
-static_assert((TG_RAW / 16) % TG_SPLIT_THREADS == 0, "split work divides evenly");
-static_assert((2 * TG_RS + 2 * TG_SS + 1) * 8 + 4 <= TG_BAR_BYTES, "barriers fit");
+constexpr int TG_EB = 4;  // epilogue groups per thread per batch
+constexpr int TG_OUT_LD = TG_BN + 4;  // staged result row, floats (conflict-free 16-B stores)
+constexpr int TG_BAR_BYTES = 128;
+constexpr size_t TG_SMEM = 1024 /* alignment slack */ + (size_t)TG_STAGES * TG_STAGE + TG_BAR_BYTES;
+static_assert(TG_BM * TG_OUT_LD * 4 <= TG_STAGES * TG_STAGE, "staged result fits the ring");
+static_assert((TG_W_BYTES / 16) % TG_WSPLIT_THREADS == 0, "split work divides evenly");
+static_assert(TG_XCOL + TG_STAGES * 2 * TG_BK <= TG_TMEM_COLS, "X buffers fit the TMEM allocation");
+static_assert((3 * TG_STAGES + 1) * 8 + 4 <= TG_BAR_BYTES, "barriers fit");
 
 // Operand tensor maps: X, then W as up to three row segments (or gate, up).
 struct TgMaps {
@@ -80,16 +93,42 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// kind::tf32 instruction descriptor: D F32, A/B TF32, both K-major, N=64, M=128.
-constexpr uint32_t TG_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TG_BN >> 3) << 17) |
-                              ((uint32_t)(TG_BM >> 4) << 24);
+// kind::tf32 instruction descriptor: D F32, A/B TF32, both K-major, M=128.
+__host__ __device__ constexpr uint32_t tg_idesc(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TG_BM >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, bool accumulate) {
+// A (X) from tensor memory, B (W) from shared memory.
+template <int N>
+__device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, bool accumulate) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(TG_IDESC), "r"((uint32_t)accumulate), "r"(0u)
+        "{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %4, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"((uint32_t)accumulate), "r"(tg_idesc(N)), "r"(0u)
         : "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),
+          "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+          "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -110,6 +149,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "[%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
+}
+
+// byte offset of 16-byte chunk c of row r in a K-major 128-byte-swizzle tile
+__device__ __forceinline__ uint32_t tg_off(int r, int c) {
+    return (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u + (uint32_t)((c ^ (r & 7)) * 16);
 }
 
 __device__ __forceinline__ float4 tg_small(float4 v) {
@@ -142,12 +186,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     // 1024-byte aligned stage buffers (the swizzle pattern repeats every 1024 B)
     unsigned char* base = tg_raw + ((1024u - (smem_u32(tg_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(base);
-    const uint32_t small0 = sbase + TG_RS * TG_RAW;
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + (TG_RS + TG_SS) * TG_RAW);  // TMA landed [RS]
-    uint64_t* empty = full + TG_RS;      // MMAs done with a raw slot [RS]
-    uint64_t* sdone = empty + TG_RS;     // `small` written [SS]
-    uint64_t* sfree = sdone + TG_SS;     // MMAs done with a small buffer [SS]
-    uint64_t* accfull = sfree + TG_SS;   // every MMA done
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + TG_STAGES * TG_STAGE);  // TMA landed [STAGES]
+    uint64_t* ready = full + TG_STAGES;    // X in TMEM and W_small written [STAGES]
+    uint64_t* empty = ready + TG_STAGES;   // MMAs done with a stage [STAGES]
+    uint64_t* accfull = empty + TG_STAGES; // every MMA done
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
     __shared__ int tg_err;
 
@@ -159,7 +201,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     const int sb = (int)((long long)z * nst / ks), se = (int)((long long)(z + 1) * nst / ks);
     const int nloc = se - sb;
 
-    // W box of a stage: 64 rows of one segment, or 32 gate + 32 up rows
+    // W box of a stage: 128 rows of one segment, or 64 gate + 64 up rows
     const CUtensorMap* wmap0;
     const CUtensorMap* wmap1 = nullptr;
     int wy;
@@ -178,37 +220,38 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
         wy = n0 - a.seg2;
     }
     auto load_w = [&](int st, int slot) {
-        const uint32_t dst = sbase + slot * TG_RAW + TG_A_BYTES;
+        const uint32_t dst = sbase + slot * TG_STAGE + TG_X_BYTES;
         if (wmap1) {
             tma_load_2d(dst, wmap0, st * TG_BK, wy, &full[slot]);
-            tma_load_2d(dst + TG_B_BYTES / 2, wmap1, st * TG_BK, wy, &full[slot]);
+            tma_load_2d(dst + TG_W_BYTES / 2, wmap1, st * TG_BK, wy, &full[slot]);
         } else {
             tma_load_2d(dst, wmap0, st * TG_BK, wy, &full[slot]);
         }
     };
 
     if (tid == 0) {
-        for (int s = 0; s < TG_RS; ++s) {
+        stamp_min(a.ts);
+        for (int s = 0; s < TG_STAGES; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&ready[s], TG_READY_WARPS);
             mbar_init(&empty[s], 1);
-        }
-        for (int s = 0; s < TG_SS; ++s) {
-            mbar_init(&sdone[s], TG_SPLIT_THREADS);
-            mbar_init(&sfree[s], 1);
         }
         mbar_init(accfull, 1);
         mbar_fence_init();
         // a split grid must run as one cluster per tile (peer reads below)
         tg_err = (ks > 1 && (int)tg_cluster_size() != ks) ? 1 : 0;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap0)) : "memory");
+        if (wmap1) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap1)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm.a)) : "memory");
         // weights of the first stages do not depend on the previous kernel
-        for (int i = 0; i < TG_RS && i < nloc; ++i) {
-            mbar_expect_tx(&full[i], TG_RAW);
+        for (int i = 0; i < TG_STAGES && i < nloc; ++i) {
+            mbar_expect_tx(&full[i], TG_X_BYTES + TG_W_BYTES);
             load_w(sb + i, i);
         }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TG_BN)
+                     "r"(TG_TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -218,88 +261,125 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     const uint32_t tmem = *tmem_slot;
 
     pdl_wait();
+    if (tid == 0) stamp_wait(a.ts);
     int err = 0;
     if (warp == 0) {
         if (lane == 0) {  // producer
-            for (int i = 0; i < TG_RS && i < nloc; ++i)
-                tma_load_2d(sbase + i * TG_RAW, &tm.a, (sb + i) * TG_BK, m0, &full[i]);
+            for (int i = 0; i < TG_STAGES && i < nloc; ++i)
+                tma_load_2d(sbase + i * TG_STAGE, &tm.a, (sb + i) * TG_BK, m0, &full[i]);
             pdl_trigger();
-            for (int i = TG_RS; i < nloc; ++i) {
-                const int s = i % TG_RS;
-                if (!mbar_wait(&empty[s], (uint32_t)((i - TG_RS) / TG_RS) & 1u, a.err)) err = 1;
-                mbar_expect_tx(&full[s], TG_RAW);
+            for (int i = TG_STAGES; i < nloc; ++i) {
+                const int s = i % TG_STAGES;
+                if (!mbar_wait(&empty[s], (uint32_t)((i - TG_STAGES) / TG_STAGES) & 1u, a.err)) err = 1;
+                mbar_expect_tx(&full[s], TG_X_BYTES + TG_W_BYTES);
                 load_w(sb + i, s);
-                tma_load_2d(sbase + s * TG_RAW, &tm.a, (sb + i) * TG_BK, m0, &full[s]);
+                tma_load_2d(sbase + s * TG_STAGE, &tm.a, (sb + i) * TG_BK, m0, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issue
             for (int i = 0; i < nloc; ++i) {
-                const int s = i % TG_RS, j = i % TG_SS;
-                if (!mbar_wait(&sdone[j], (uint32_t)(i / TG_SS) & 1u, a.err)) err = 1;
+                const int s = i % TG_STAGES;
+                if (!mbar_wait(&ready[s], (uint32_t)(i / TG_STAGES) & 1u, a.err)) err = 1;
+                if (i == 0 && a.ts) {
+                    stamp_max(a.ts + 4);
+                    stamp_min(a.ts + 8);
+                }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t ab = sbase + s * TG_RAW, bb = ab + TG_A_BYTES;
-                const uint32_t as_ = small0 + j * TG_RAW, bs = as_ + TG_A_BYTES;
+                const uint32_t wb = sbase + s * TG_STAGE + TG_X_BYTES;  // W_big, W_small follows
+                const uint32_t xb = tmem + TG_XCOL + (uint32_t)s * 2 * TG_BK, xs = xb + TG_BK;
 #pragma unroll
                 for (int kk = 0; kk < TG_BK / 8; ++kk) {
-                    const uint32_t o = kk * 32;  // 8 TF32 = 32 bytes along K
-                    umma_tf32(tmem, umma_desc_sw128(ab + o), umma_desc_sw128(bb + o), i > 0 || kk > 0);
-                    umma_tf32(tmem, umma_desc_sw128(ab + o), umma_desc_sw128(bs + o), true);
-                    umma_tf32(tmem, umma_desc_sw128(as_ + o), umma_desc_sw128(bb + o), true);
+                    // 8 TF32 per k-step: 32 bytes along K in shared memory, 8 TMEM columns
+                    const uint64_t dw = umma_desc_sw128(wb + kk * 32);
+                    umma_tf32_ts<2 * TG_BN>(tmem, xb + kk * 8, dw, i > 0 || kk > 0);
+                    umma_tf32_ts<TG_BN>(tmem, xs + kk * 8, dw, true);
                 }
                 umma_commit(&empty[s]);
-                umma_commit(&sfree[j]);
             }
             if (nloc > 0) umma_commit(accfull);
         }
-    } else {  // split
+    } else if (warp < 4) {  // W split
         const int t = tid - 64;
         for (int i = 0; i < nloc; ++i) {
-            const int s = i % TG_RS, j = i % TG_SS;
-            if (!mbar_wait(&full[s], (uint32_t)(i / TG_RS) & 1u, a.err)) err = 1;
-            if (i >= TG_SS && !mbar_wait(&sfree[j], (uint32_t)((i - TG_SS) / TG_SS) & 1u, a.err)) err = 1;
-            const float4* raw = reinterpret_cast<const float4*>(base + s * TG_RAW);
-            float4* sml = reinterpret_cast<float4*>(base + (TG_RS + j) * TG_RAW);
+            const int s = i % TG_STAGES;
+            if (lane == 0 && !mbar_wait(&full[s], (uint32_t)(i / TG_STAGES) & 1u, a.err)) err = 1;
+            __syncwarp();
+            const float4* wr = reinterpret_cast<const float4*>(base + s * TG_STAGE + TG_X_BYTES);
+            float4* ws = reinterpret_cast<float4*>(base + s * TG_STAGE + TG_X_BYTES + TG_W_BYTES);
 #pragma unroll
-            for (int q = 0; q < TG_RAW / 16 / TG_SPLIT_THREADS; ++q)
-                sml[t + TG_SPLIT_THREADS * q] = tg_small(raw[t + TG_SPLIT_THREADS * q]);
+            for (int q = 0; q < TG_W_BYTES / 16 / TG_WSPLIT_THREADS; ++q)
+                ws[t + TG_WSPLIT_THREADS * q] = tg_small(wr[t + TG_WSPLIT_THREADS * q]);
             // generic-proxy shared writes -> visible to the tensor core (async proxy)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tg_arrive(&sdone[j]);
+            __syncwarp();
+            if (lane == 0) tg_arrive(&ready[s]);
+        }
+    } else {  // X rows -> TMEM (warp w owns TMEM lanes 32*(w%4)..)
+        const int r = 32 * (warp & 3) + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        for (int i = 0; i < nloc; ++i) {
+            const int s = i % TG_STAGES;
+            if (lane == 0 && !mbar_wait(&full[s], (uint32_t)(i / TG_STAGES) & 1u, a.err)) err = 1;
+            __syncwarp();
+            // The stage's TMEM buffer is free: its previous MMAs completed
+            // before the producer refilled this slot.
+            const unsigned char* raw = base + s * TG_STAGE;
+            uint32_t big[32], sml[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 v = *reinterpret_cast<const float4*>(raw + tg_off(r, c));
+                const float4 w = tg_small(v);
+                big[4 * c] = __float_as_uint(v.x);
+                big[4 * c + 1] = __float_as_uint(v.y);
+                big[4 * c + 2] = __float_as_uint(v.z);
+                big[4 * c + 3] = __float_as_uint(v.w);
+                sml[4 * c] = __float_as_uint(w.x);
+                sml[4 * c + 1] = __float_as_uint(w.y);
+                sml[4 * c + 2] = __float_as_uint(w.z);
+                sml[4 * c + 3] = __float_as_uint(w.w);
+            }
+            const uint32_t col = lane_addr + TG_XCOL + (uint32_t)s * 2 * TG_BK;
+            tmem_st32(col, big);
+            tmem_st32(col + TG_BK, sml);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) tg_arrive(&ready[s]);
         }
     }
     __syncwarp();
     // all MMAs done (so every TMA load was consumed)
-    if (nloc > 0 && !mbar_wait(accfull, 0u, a.err)) err = 1;
+    if (lane == 0 && nloc > 0 && !mbar_wait(accfull, 0u, a.err)) err = 1;
+    if (tid == 0) stamp_max(a.ts ? a.ts + 5 : nullptr);
+    __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-    // accumulator -> shared tile [128][TG_OUT_LD]: warp w reads TMEM lanes
-    // 32*(w%4).. (tile rows) and columns 32*(w/4)..
-    const int rq = warp & 3, ch = warp >> 2;
-    uint32_t r32[32];
-    const uint32_t taddr = tmem + ((uint32_t)(32 * rq) << 16) + (uint32_t)(32 * ch);
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r32[0]), "=r"(r32[1]), "=r"(r32[2]), "=r"(r32[3]), "=r"(r32[4]), "=r"(r32[5]), "=r"(r32[6]),
-          "=r"(r32[7]), "=r"(r32[8]), "=r"(r32[9]), "=r"(r32[10]), "=r"(r32[11]), "=r"(r32[12]), "=r"(r32[13]),
-          "=r"(r32[14]), "=r"(r32[15]), "=r"(r32[16]), "=r"(r32[17]), "=r"(r32[18]), "=r"(r32[19]),
-          "=r"(r32[20]), "=r"(r32[21]), "=r"(r32[22]), "=r"(r32[23]), "=r"(r32[24]), "=r"(r32[25]),
-          "=r"(r32[26]), "=r"(r32[27]), "=r"(r32[28]), "=r"(r32[29]), "=r"(r32[30]), "=r"(r32[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    if (nloc == 0) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r32[j] = 0u;  // no K range: a zero partial
-    }
-    float* acc_s = reinterpret_cast<float*>(base);  // the raw ring is idle now
+    // result -> shared tile [128][TG_OUT_LD]: warp w reads TMEM lanes
+    // 32*(w%4).. (tile rows) and result columns 64*(w/4).. as D[c] + D[128+c]
+    const int rq = warp & 3, hf = warp >> 2;
+    float* acc_s = reinterpret_cast<float*>(base);  // the ring is idle now
     {
-        float* row = acc_s + (32 * rq + lane) * TG_OUT_LD + 32 * ch;
+        const uint32_t lrow = tmem + ((uint32_t)(32 * rq) << 16);
+        float* row = acc_s + (32 * rq + lane) * TG_OUT_LD;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            const int c0 = 64 * hf + 32 * h;
+            uint32_t d1[32], d2[32];
+            tmem_ld32(lrow + (uint32_t)c0, d1);
+            tmem_ld32(lrow + (uint32_t)(TG_BN + c0), d2);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(row + 4 * q) =
-                make_float4(__uint_as_float(r32[4 * q]), __uint_as_float(r32[4 * q + 1]),
-                            __uint_as_float(r32[4 * q + 2]), __uint_as_float(r32[4 * q + 3]));
+            for (int q = 0; q < 8; ++q) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (nloc > 0)  // no K range: a zero partial
+                    v = make_float4(__uint_as_float(d1[4 * q]) + __uint_as_float(d2[4 * q]),
+                                    __uint_as_float(d1[4 * q + 1]) + __uint_as_float(d2[4 * q + 1]),
+                                    __uint_as_float(d1[4 * q + 2]) + __uint_as_float(d2[4 * q + 2]),
+                                    __uint_as_float(d1[4 * q + 3]) + __uint_as_float(d2[4 * q + 3]));
+                *reinterpret_cast<float4*>(row + c0 + 4 * q) = v;
+            }
+        }
     }
     if (err) atomicExch(&tg_err, 1);
     const bool split = ks > 1;
@@ -308,12 +388,13 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     else
         __syncthreads();
     const bool peers_ok = !split || tg_err == 0;
+    if (tid == 0) stamp_max(a.ts ? a.ts + 6 : nullptr);
 
-    // 16-byte groups of the output: rows x 16 (rows x 8 for SwiGLU, whose
-    // group c pairs gate columns 4c.. with up columns 32+4c..); CTA z of a
+    // 16-byte groups of the output: rows x 32 (rows x 16 for SwiGLU, whose
+    // group c pairs gate columns 4c.. with up columns 64+4c..); CTA z of a
     // split tile owns groups [z*G/ks, (z+1)*G/ks)
     const bool glu = a.mode == 3;
-    const int per_row = glu ? 8 : 16;
+    const int per_row = glu ? TG_BN / 8 : TG_BN / 4;
     const int G = TG_BM * per_row;
     const int g_lo = split ? (int)((long long)z * G / ks) : 0;
     const int g_hi = split ? (int)((long long)(z + 1) * G / ks) : G;
@@ -321,69 +402,102 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     const bool vec_res =
         a.mode != 1 || (((a.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.resid) & 15) == 0));
     const int ncols = glu ? a.N >> 1 : a.N;  // output columns
-    const int c0 = glu ? n0 >> 1 : n0;
-    for (int g = g_lo + tid; g < g_hi; g += TG_THREADS) {
-        const int r = g / per_row, c4 = g % per_row;
-        const int m = m0 + r, n = c0 + 4 * c4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = v;
-        const float* src = acc_s + r * TG_OUT_LD + 4 * c4;
-        if (!split) {
-            v = *reinterpret_cast<const float4*>(src);
-            if (glu) u = *reinterpret_cast<const float4*>(src + 32);
-        } else if (peers_ok) {
-            const uint32_t la = smem_u32(src);
-            for (int zz = 0; zz < ks; ++zz) {
-                const float4 p = tg_ld_peer4(la, (uint32_t)zz);
-                v.x += p.x, v.y += p.y, v.z += p.z, v.w += p.w;
-                if (glu) {
-                    const float4 q = tg_ld_peer4(la + 128u, (uint32_t)zz);
-                    u.x += q.x, u.y += q.y, u.z += q.z, u.w += q.w;
+    const int oc0 = glu ? n0 >> 1 : n0;
+    // Groups are handled TG_EB at a time with every load of the batch (peer
+    // partials, residual) issued before any is used: one memory round trip
+    // per batch instead of one per load.
+    for (int g0 = g_lo + tid; g0 < g_hi; g0 += TG_THREADS * TG_EB) {
+        float4 v[TG_EB], u[TG_EB], q[TG_EB];
+#pragma unroll
+        for (int b = 0; b < TG_EB; ++b) {
+            const int g = g0 + b * TG_THREADS;
+            v[b] = u[b] = q[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (g >= g_hi) continue;
+            const int r = g / per_row, c4 = g % per_row;
+            const int m = m0 + r, n = oc0 + 4 * c4;
+            if (a.mode == 1 && m < a.T && n + 3 < ncols && vec_res)
+                q[b] = __ldcg(reinterpret_cast<const float4*>(a.resid + (size_t)m * a.ldr + n));
+        }
+#pragma unroll
+        for (int b = 0; b < TG_EB; ++b) {
+            const int g = g0 + b * TG_THREADS;
+            if (g >= g_hi) continue;
+            const int r = g / per_row, c4 = g % per_row;
+            const float* src = acc_s + r * TG_OUT_LD + 4 * c4;
+            if (!split) {
+                v[b] = *reinterpret_cast<const float4*>(src);
+                if (glu) u[b] = *reinterpret_cast<const float4*>(src + TG_BN / 2);
+            } else if (peers_ok) {
+                const uint32_t la = smem_u32(src);
+                float4 p[TG_MAX_SPLITS], pu[TG_MAX_SPLITS];
+#pragma unroll
+                for (int zz = 0; zz < TG_MAX_SPLITS; ++zz) {
+                    if (zz < ks) {
+                        p[zz] = tg_ld_peer4(la, (uint32_t)zz);
+                        if (glu) pu[zz] = tg_ld_peer4(la + TG_BN / 2 * 4, (uint32_t)zz);
+                    }
+                }
+#pragma unroll
+                for (int zz = 0; zz < TG_MAX_SPLITS; ++zz) {  // split order
+                    if (zz < ks) {
+                        v[b].x += p[zz].x, v[b].y += p[zz].y, v[b].z += p[zz].z, v[b].w += p[zz].w;
+                        if (glu) u[b].x += pu[zz].x, u[b].y += pu[zz].y, u[b].z += pu[zz].z, u[b].w += pu[zz].w;
+                    }
                 }
             }
         }
-        if (m >= a.T || tg_err) continue;
-        float e[4] = {v.x, v.y, v.z, v.w};
-        if (glu) {
-            e[0] = silu(v.x) * u.x;
-            e[1] = silu(v.y) * u.y;
-            e[2] = silu(v.z) * u.z;
-            e[3] = silu(v.w) * u.w;
-        }
-        float* orow = a.out + (size_t)m * a.ldo;
-        if (n + 3 < ncols && vec_out && vec_res) {
-            if (a.mode == 1) {
-                const float4 q = __ldcg(reinterpret_cast<const float4*>(a.resid + (size_t)m * a.ldr + n));
-                e[0] += q.x, e[1] += q.y, e[2] += q.z, e[3] += q.w;
-            } else if (a.mode == 2) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) e[k] += __ldg(a.bias + n + k);
+        for (int b = 0; b < TG_EB; ++b) {
+            const int g = g0 + b * TG_THREADS;
+            if (g >= g_hi || tg_err) continue;
+            const int r = g / per_row, c4 = g % per_row;
+            const int m = m0 + r, n = oc0 + 4 * c4;
+            if (m >= a.T) continue;
+            float e[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+            if (glu) {
+                e[0] = silu(v[b].x) * u[b].x;
+                e[1] = silu(v[b].y) * u[b].y;
+                e[2] = silu(v[b].z) * u[b].z;
+                e[3] = silu(v[b].w) * u[b].w;
             }
-            *reinterpret_cast<float4*>(orow + n) = make_float4(e[0], e[1], e[2], e[3]);
-        } else {
+            float* orow = a.out + (size_t)m * a.ldo;
+            if (n + 3 < ncols && vec_out && vec_res) {
+                if (a.mode == 1) {
+                    e[0] += q[b].x, e[1] += q[b].y, e[2] += q[b].z, e[3] += q[b].w;
+                } else if (a.mode == 2) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (n + k >= ncols) break;
-                float val = e[k];
-                if (a.mode == 1) val += __ldcg(a.resid + (size_t)m * a.ldr + n + k);
-                if (a.mode == 2) val += __ldg(a.bias + n + k);
-                orow[n + k] = val;
+                    for (int k = 0; k < 4; ++k) e[k] += __ldg(a.bias + n + k);
+                }
+                *reinterpret_cast<float4*>(orow + n) = make_float4(e[0], e[1], e[2], e[3]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (n + k >= ncols) break;
+                    float val = e[k];
+                    if (a.mode == 1) val += __ldcg(a.resid + (size_t)m * a.ldr + n + k);
+                    if (a.mode == 2) val += __ldg(a.bias + n + k);
+                    orow[n + k] = val;
+                }
             }
         }
     }
     if (tid == 0) {
+        stamp_max(a.ts ? a.ts + 7 : nullptr);
         // no copy may still be landing when the CTA exits (only reachable
         // after a timed-out wait; these phases are complete otherwise)
-        for (int i = nloc > TG_RS ? nloc - TG_RS : 0; i < nloc; ++i)
-            mbar_wait(&full[i % TG_RS], (uint32_t)(i / TG_RS) & 1u, a.err);
+        for (int i = nloc > TG_STAGES ? nloc - TG_STAGES : 0; i < nloc; ++i)
+            mbar_wait(&full[i % TG_STAGES], (uint32_t)(i / TG_STAGES) & 1u, a.err);
         if (tg_err && a.err != nullptr) atomicExch(a.err, 1);
     }
     // peers may still read this CTA's tile
     if (split) asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-    // release the accumulator
+    // release tensor memory
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TG_BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TG_TMEM_COLS)
+                     : "memory");
+    if (tid == 0) stamp_max(a.ts ? a.ts + 3 : nullptr);
 }
 
 namespace {
@@ -466,7 +580,8 @@ int tgemm_splits(const GemmArgs& a) {
 }
 
 // K a multiple of 32; X, W and the row strides 16-byte aligned; SwiGLU
-// (interleave) needs N a multiple of 64, row segments start at multiples of 64.
+// (interleave) needs N a multiple of 128, row segments start at multiples of
+// 128.
 cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl) {
     const cudaError_t pe = tgemm_prepare();
     if (pe != cudaSuccess) return pe;

@@ -74,6 +74,11 @@ struct GemmArgs {
     int mode;  // 0 store, 1 resid, 2 bias, 3 swiglu
     int* err;  // optional: set when a wait timed out (tensor-core GEMM)
     int splits;  // tensor-core GEMM: K splits per output tile (0 = chosen by occupancy)
+    // tensor-core GEMM debug timeline (null: off): [0..3] as for every
+    // kernel, [4] latest / [8] earliest first stage at the MMA, [5] latest
+    // all-MMAs-done, [6] latest result staged (after the cluster barrier),
+    // [7] latest output stores issued
+    unsigned long long* ts;
 };
 
 
