@@ -308,11 +308,9 @@ def b200_main(args, wl):
         torch.cuda.synchronize()
 
     def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        from soraku_tts_b200.batching import max_over_ranks as mor
+
+        return mor(v, device="cuda")
 
     # warm-up through the public API (builds the engine and its graph)
     for w in range(args.warmup):
@@ -429,16 +427,11 @@ def config4_requests(n_req: int, text, ref):
 
 
 def split_requests(reqs, frames: int, world: int):
-    """Static split balanced on (prompt length + frames): longest first, each
-    to the least-loaded rank."""
-    order = sorted(range(len(reqs)), key=lambda i: -(reqs[i][0].shape[1] + reqs[i][2].shape[0] + frames))
-    load = [0] * world
-    parts = [[] for _ in range(world)]
-    for i in order:
-        w = min(range(world), key=lambda k: load[k])
-        parts[w].append(i)
-        load[w] += reqs[i][0].shape[1] + reqs[i][2].shape[0] + frames
-    return [sorted(p) for p in parts]
+    """Static split balanced on the KV positions a request keeps (prompt
+    length + frames)."""
+    from soraku_tts_b200.batching import split_requests as split
+
+    return split([r[0].shape[1] + r[2].shape[0] + frames for r in reqs], world)
 
 
 def config4_main(args, wl):
@@ -522,9 +515,17 @@ def config4_main(args, wl):
     dec_s = max_over_ranks(sum(dec_ms) / 1e3)
     total_frames = wl["requests"] * frames * args.steps
     value = total_frames / dec_s
-    for j in range(n):
-        c = eng.read_codes(j, 0, frames)
+    # results: every request's codes on rank 0 (outside the timed region)
+    from soraku_tts_b200.batching import gather_codes
+
+    local = {}
+    for j, i in enumerate(mine):
+        c = eng.read_codes(j, 0, frames).cpu().numpy()
         assert c.shape == (frames, 16) and int(c.max()) < 2048 and int(c.min()) >= 0
+        local[i] = c
+    merged = gather_codes(local)
+    if rank == 0:
+        assert sorted(merged) == list(range(wl["requests"])), "a request produced no codes"
 
     # end to end: prefill from host ids, decode, codes back to host
     barrier()
