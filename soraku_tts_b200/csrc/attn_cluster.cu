@@ -13,10 +13,15 @@
 // round trip).  Scores, softmax and P.V run on shared memory; the C partial
 // (max, sum, output) triples are merged in split order by the cluster's rank
 // 0 through distributed shared memory, so no global partials, atomics or
-// second launch are needed.  Ranges longer than ATC_PMAX positions are
-// processed in rounds with an online softmax.
+// second launch are needed.  Ranges longer than PMAX positions are processed
+// in rounds with an online softmax.
 //
-// (The merge area, ATC_MAXC partials, lives in rank 0's K buffer.)
+// Two variants: for few (row, kv head) groups (batch-1 CFG: 16) a CTA stages
+// 112 positions per round into one buffer (one CTA per SM, wide clusters);
+// for many groups (batched rows) a CTA double-buffers rounds of 48 positions
+// (two CTAs per SM), so the next round's copies overlap this round's math.
+//
+// (The merge area, ATC_MAXC partials, lives in rank 0's first K buffer.)
 //
 // Arithmetic restates transformers' Qwen3 attention step (modeling_qwen3.py:
 // q_norm/k_norm :248-249, RoPE :130-181, GQA softmax :184-219, scaling
@@ -28,23 +33,28 @@
 namespace skb {
 
 constexpr int ATC_THREADS = 256;
-constexpr int ATC_PMAX = 112;  // cached positions staged per round
 constexpr int ATC_MAXC = 8;    // CTAs per cluster (portable cluster size)
 constexpr int ATC_PART = 260;  // floats of one pushed partial: o[2][128], m[2], l[2]
+// variants: (positions per round, buffers)
+constexpr int ATC_PMAX_FEW = 112, ATC_NBUF_FEW = 1;
+constexpr int ATC_PMAX_MANY = 48, ATC_NBUF_MANY = 2;
+constexpr int ATC_MANY_GROUPS = 32;  // more (row, kv head) groups than this: the double-buffered variant
 
+template <int PMAX, int NBUF>
 struct AtcSmem {
-    float k[ATC_PMAX][128];
-    float v[ATC_PMAX][128];
+    float k[NBUF][PMAX][128];
+    float v[NBUF][PMAX][128];
     float q[2][128];
     float kn[128];
     float vn[128];
-    float p[2][ATC_PMAX + 4];  // scores, then probabilities (+ the new position)
-    float mr[2], lr[2];        // per-round block max / sum
-    uint64_t bar;
+    float p[2][PMAX + 4];  // scores, then probabilities (+ the new position)
+    float mr[2], lr[2];    // per-round block max / sum
+    uint64_t bar[NBUF];
     uint64_t merge_bar;  // rank 0: every CTA's partial has arrived
     int err;
 };
-static_assert(ATC_MAXC * ATC_PART <= ATC_PMAX * 128, "merge area must fit in the K buffer");
+static_assert(ATC_MAXC * ATC_PART <= ATC_PMAX_MANY * 128, "merge area must fit in the K buffer");
+static_assert(8 * 2 * 128 <= ATC_PMAX_MANY * 128, "warp sums must fit in the K buffer");
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -70,8 +80,11 @@ __device__ __forceinline__ void st_async_f32(float* p, float v, uint64_t* bar, u
 }
 
 // Issues the bulk copies of cached positions [p0, p1) of (row r, head g)
-// into sm.k / sm.v (index = position - p0); returns the bytes requested.
-__device__ uint32_t atc_stage(const DecodeAttnArgs& a, int r, int g, int p0, int p1, AtcSmem& sm) {
+// into buffer b of sm.k / sm.v (index = position - p0); returns the bytes
+// requested.
+template <int PMAX, int NBUF>
+__device__ uint32_t atc_stage(const DecodeAttnArgs& a, int r, int g, int p0, int p1, AtcSmem<PMAX, NBUF>& sm,
+                              int b) {
     uint32_t bytes = 0;
     const int page_sz = 1 << a.kv.page_log2;
     int p = p0;
@@ -81,7 +94,7 @@ __device__ uint32_t atc_stage(const DecodeAttnArgs& a, int r, int g, int p0, int
         p = end;
     }
     if (bytes == 0) return 0;
-    mbar_expect_tx(&sm.bar, bytes);
+    mbar_expect_tx(&sm.bar[b], bytes);
     p = p0;
     while (p < p1) {
         const int end = min(p1, ((p >> a.kv.page_log2) + 1) * page_sz);
@@ -92,16 +105,17 @@ __device__ uint32_t atc_stage(const DecodeAttnArgs& a, int r, int g, int p0, int
                           ((((long long)page * 2 + 0) * a.kv.KVH + g) << a.kv.page_log2) * 128 + (long long)slot * 128;
         const float* vb = kb + ((long long)a.kv.KVH << a.kv.page_log2) * 128;
         const uint32_t nb = (uint32_t)(end - p) * 512u;
-        bulk_g2s(&sm.k[p - p0][0], kb, nb, &sm.bar);
-        bulk_g2s(&sm.v[p - p0][0], vb, nb, &sm.bar);
+        bulk_g2s(&sm.k[b][p - p0][0], kb, nb, &sm.bar[b]);
+        bulk_g2s(&sm.v[b][p - p0][0], vb, nb, &sm.bar[b]);
         p = end;
     }
     return bytes;
 }
 
+template <int PMAX, int NBUF>
 __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const DecodeAttnArgs a) {
     extern __shared__ __align__(128) unsigned char atc_raw[];
-    AtcSmem& sm = *reinterpret_cast<AtcSmem*>(atc_raw);
+    AtcSmem<PMAX, NBUF>& sm = *reinterpret_cast<AtcSmem<PMAX, NBUF>*>(atc_raw);
     const int s = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
     const int C = gridDim.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -112,7 +126,7 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     unsigned long long tl[7] = {0, 0, 0, 0, 0, 0, 0};
     if (tid == 0) {
         stamp_min(a.ts);
-        mbar_init(&sm.bar, 1);
+        for (int b = 0; b < NBUF; ++b) mbar_init(&sm.bar[b], 1);
         mbar_init(&sm.merge_bar, 1);
         mbar_fence_init();
         // rank 0 expects C partials of n_rep * (128 + 2) floats
@@ -131,11 +145,19 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     const bool own_new = pe == T;            // the last CTA holds position p_new
     const int cend = own_new ? p_new : pe;   // cached positions [pb, cend)
     const int n_cached = cend > pb ? cend - pb : 0;
-    const int n_rounds = n_cached > 0 ? (n_cached + ATC_PMAX - 1) / ATC_PMAX : 1;
+    const int n_rounds = n_cached > 0 ? (n_cached + PMAX - 1) / PMAX : 1;
+    // copies issued / waited per buffer (thread 0's count): a buffer whose
+    // last copy was not seen to land is waited on once more before exit
+    int n_issued[NBUF], n_waited[NBUF];
+#pragma unroll
+    for (int b = 0; b < NBUF; ++b) n_issued[b] = n_waited[b] = 0;
     if (tid == 0) {
-        atc_stage(a, r, g, pb, pb + min(n_cached, ATC_PMAX), sm);
+        for (int b = 0; b < NBUF && b < n_rounds; ++b) {
+            const int p0 = pb + b * PMAX;
+            if (atc_stage(a, r, g, p0, min(cend, p0 + PMAX), sm, b) > 0) ++n_issued[b];
+        }
         // later rounds (long contexts): into L2 now, into shared memory later
-        for (int p = pb + ATC_PMAX; p < cend;) {
+        for (int p = pb + NBUF * PMAX; p < cend;) {
             const int end = min(cend, ((p >> a.kv.page_log2) + 1) << a.kv.page_log2);
             const float* kb = a.kv.at(a.layer, r, p, 0, g);
             const float* vb = a.kv.at(a.layer, r, p, 1, g);
@@ -179,7 +201,7 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     __syncthreads();
     tl[0] = a.ts ? globaltimer_ns() : 0;
 
-    // ---- rounds of up to ATC_PMAX cached positions (+ p_new in the last)
+    // ---- rounds of up to PMAX cached positions (+ p_new in the last)
     // Scores: lane 8G+t of a warp works on slot i0+G and float4 columns
     // t, t+8, t+16, t+24 of the K row (each 8-lane phase of a 128-bit shared
     // load reads 128 contiguous bytes: no bank conflicts), reduced over the
@@ -196,24 +218,25 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     const int pc = lane, gp = warp;
     float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    uint32_t phase = 0;
     for (int rd = 0; rd < n_rounds; ++rd) {
         // a copy that timed out stops the rounds (sm.err was written before
         // the last barrier, so every thread takes the same branch)
         if (sm.err) break;
-        const int r0 = pb + rd * ATC_PMAX;
-        const int nc = max(0, min(ATC_PMAX, cend - r0));  // cached positions this round
+        const int b = rd % NBUF;
+        const int r0 = pb + rd * PMAX;
+        const int nc = max(0, min(PMAX, cend - r0));  // cached positions this round
         const bool last = rd == n_rounds - 1;
         const int ns = nc + ((last && own_new) ? 1 : 0);  // score slots
-        if (rd > 0 && tid == 0) atc_stage(a, r, g, r0, r0 + nc, sm);
+        if (NBUF == 1 && rd > 0 && tid == 0 && atc_stage(a, r, g, r0, r0 + nc, sm, 0) > 0) ++n_issued[0];
         if (nc > 0) {
-            if (!mbar_wait(&sm.bar, phase, a.err)) sm.err = 1;
-            phase ^= 1u;
+            // the round's copy is use number rd / NBUF of its buffer
+            if (!mbar_wait(&sm.bar[b], (uint32_t)(rd / NBUF) & 1u, a.err)) sm.err = 1;
+            ++n_waited[b];
         }
         if (rd == 0) tl[1] = a.ts ? globaltimer_ns() : 0;
         for (int i0 = warp * 4; i0 < ns; i0 += 32) {
             const int i = i0 + sg;
-            const float4* kr = reinterpret_cast<const float4*>(i < nc ? sm.k[i < nc ? i : 0] : sm.kn);
+            const float4* kr = reinterpret_cast<const float4*>(i < nc ? sm.k[b][i < nc ? i : 0] : sm.kn);
             float s0 = 0.f, s1 = 0.f;
             if (i < ns) {
 #pragma unroll
@@ -277,7 +300,7 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             for (int i = gp; i < ns; i += 8) {
                 const float p0 = sm.p[0][i];
                 const float p1 = n_rep > 1 ? sm.p[1][i] : 0.f;
-                const float4 vv = reinterpret_cast<const float4*>(i < nc ? sm.v[i < nc ? i : 0] : sm.vn)[pc];
+                const float4 vv = reinterpret_cast<const float4*>(i < nc ? sm.v[b][i < nc ? i : 0] : sm.vn)[pc];
                 acc0.x = fmaf(p0, vv.x, acc0.x);
                 acc0.y = fmaf(p0, vv.y, acc0.y);
                 acc0.z = fmaf(p0, vv.z, acc0.z);
@@ -289,9 +312,14 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             }
         }
         __syncthreads();  // sm.k / sm.v / sm.p are refilled by the next round
+        // double buffering: this buffer takes round rd + NBUF
+        if (NBUF > 1 && tid == 0 && rd + NBUF < n_rounds) {
+            const int q0 = pb + (rd + NBUF) * PMAX;
+            if (atc_stage(a, r, g, q0, min(cend, q0 + PMAX), sm, b) > 0) ++n_issued[b];
+        }
     }
     // the 8 warps' sums, added in warp order (K buffer as scratch)
-    float* gsum = &sm.k[0][0];  // [8][2][128]
+    float* gsum = &sm.k[0][0][0];  // [8][2][128]
     reinterpret_cast<float4*>(gsum + (gp * 2 + 0) * 128)[pc] = acc0;
     reinterpret_cast<float4*>(gsum + (gp * 2 + 1) * 128)[pc] = acc1;
     __syncthreads();
@@ -310,15 +338,18 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     // down rank 0's merge barrier; rank 0 merges them in split order.
     if (tid == 0 && sm.err) {
         // a copy did not arrive in time: flag it and wait (bounded) once more
-        // so that no copy is still in flight when the buffers are reused
+        // on every buffer's last copy so that none is still in flight when
+        // the buffers are reused
         if (a.err != nullptr) atomicExch(a.err, 1);
-        mbar_wait(&sm.bar, phase ^ 1u, nullptr);
+#pragma unroll
+        for (int b = 0; b < NBUF; ++b)
+            if (n_issued[b] > 0) mbar_wait(&sm.bar[b], (uint32_t)(n_issued[b] - 1) & 1u, nullptr);
     }
     __syncthreads();  // the group sums in the K buffer are read
     cluster_sync_exec();
     tl[5] = a.ts ? globaltimer_ns() : 0;
     const uint32_t rank = cluster_ctarank();
-    float* slot = &sm.k[0][0] + (size_t)rank * ATC_PART;  // [2][128] o | [2] m | [2] l
+    float* slot = &sm.k[0][0][0] + (size_t)rank * ATC_PART;  // [2][128] o | [2] m | [2] l
     if (hh < n_rep) {
         st_async_f32(slot + hh * 128 + d, o_run, &sm.merge_bar, 0);
         if (d == 0) {
@@ -330,7 +361,7 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
         const bool ok = mbar_wait(&sm.merge_bar, 0, a.err);
         tl[6] = a.ts ? globaltimer_ns() : 0;
         if (ok) {
-            const float* parts = &sm.k[0][0];
+            const float* parts = &sm.k[0][0][0];
             float M = -INFINITY;
             for (int j = 0; j < C; ++j) M = fmaxf(M, parts[j * ATC_PART + 256 + hh]);
             float L = 0.f, O = 0.f;
@@ -357,8 +388,15 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
     }
 }
 
+using AtcFew = AtcSmem<ATC_PMAX_FEW, ATC_NBUF_FEW>;
+using AtcMany = AtcSmem<ATC_PMAX_MANY, ATC_NBUF_MANY>;
+#define ATC_KERNEL_FEW decode_attn_cluster_kernel<ATC_PMAX_FEW, ATC_NBUF_FEW>
+#define ATC_KERNEL_MANY decode_attn_cluster_kernel<ATC_PMAX_MANY, ATC_NBUF_MANY>
+
 cudaError_t decode_attn_cluster_prepare() {
-    return set_smem_attrs(decode_attn_cluster_kernel, sizeof(AtcSmem));
+    cudaError_t e = set_smem_attrs(ATC_KERNEL_FEW, sizeof(AtcFew));
+    if (e == cudaSuccess) e = set_smem_attrs(ATC_KERNEL_MANY, sizeof(AtcMany));
+    return e;
 }
 
 // Widest cluster (<= 8 CTAs) for which `groups` clusters can be resident at
@@ -369,11 +407,12 @@ int decode_attn_cluster_width(int groups) {
         cudaGetLastError();
         return 1;
     }
+    const bool many = groups > ATC_MANY_GROUPS;
     for (int c = ATC_MAXC; c > 1; --c) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(c, 1, 1);
         cfg.blockDim = dim3(ATC_THREADS);
-        cfg.dynamicSmemBytes = sizeof(AtcSmem);
+        cfg.dynamicSmemBytes = many ? sizeof(AtcMany) : sizeof(AtcFew);
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
         at[0].val.clusterDim.x = c;
@@ -382,7 +421,9 @@ int decode_attn_cluster_width(int groups) {
         cfg.attrs = at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, decode_attn_cluster_kernel, &cfg) != cudaSuccess) {
+        const cudaError_t e = many ? cudaOccupancyMaxActiveClusters(&n, ATC_KERNEL_MANY, &cfg)
+                                   : cudaOccupancyMaxActiveClusters(&n, ATC_KERNEL_FEW, &cfg);
+        if (e != cudaSuccess) {
             cudaGetLastError();
             continue;
         }
@@ -400,10 +441,11 @@ cudaError_t decode_attn_cluster_launch(const DecodeAttnArgs& a, int R, cudaStrea
         prepared = true;
     }
     if (a.S < 1 || a.S > ATC_MAXC || a.n_rep < 1 || a.n_rep > 2 || a.kv.hd != 128) return cudaErrorInvalidValue;
+    const bool many = R * a.kv.KVH > ATC_MANY_GROUPS;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.S, a.kv.KVH, R);
     cfg.blockDim = dim3(ATC_THREADS);
-    cfg.dynamicSmemBytes = sizeof(AtcSmem);
+    cfg.dynamicSmemBytes = many ? sizeof(AtcMany) : sizeof(AtcFew);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -414,7 +456,7 @@ cudaError_t decode_attn_cluster_launch(const DecodeAttnArgs& a, int R, cudaStrea
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel, a);
+    return many ? cudaLaunchKernelEx(&cfg, ATC_KERNEL_MANY, a) : cudaLaunchKernelEx(&cfg, ATC_KERNEL_FEW, a);
 }
 
 }  // namespace skb

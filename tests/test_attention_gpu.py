@@ -2,7 +2,7 @@
 restatement of the Qwen3 attention step: q/k RMSNorm, neox RoPE, KV append at
 the row's position, GQA softmax attention -- within rel/abs 1e-4, on a paged
 cache whose page table is a permutation, for several split counts (including
-more splits than positions)."""
+more splits than positions), with 2 rows and with 10 ragged rows."""
 
 from __future__ import annotations
 
@@ -78,6 +78,21 @@ def test_decode_attention_matches_oracle(lengths, splits):
     for r, p in enumerate(c["pos"]):
         page = c["perm"][r, p // P]
         np.testing.assert_allclose(pool[page, 0, :, p % P], k_new[r], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(pool[page, 1, :, p % P], v_new[r], rtol=0, atol=0)
+
+
+# More than 4 rows (> 32 (row, kv head) groups) take the double-buffered
+# variant (rounds of 48 positions): lengths around the round edges, a row
+# with no cached position, and rows long enough for several rounds per CTA.
+@pytest.mark.parametrize("splits", [1, 2, 8])
+def test_decode_attention_many_rows_double_buffered(splits):
+    lengths = [0, 1, 47, 48, 49, 96, 97, 300, 511, 144]
+    c = make_case(lengths, seed=11 + splits)
+    got, pool = run(c, splits)
+    want, k_new, v_new = oracle(c)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+    for r, p in enumerate(c["pos"]):
+        page = c["perm"][r, p // P]
         np.testing.assert_allclose(pool[page, 1, :, p % P], v_new[r], rtol=0, atol=0)
 
 
