@@ -70,6 +70,11 @@ def parse_args():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="time only the dominant kernel (for ncu captures)")
+    ap.add_argument("--profile-frame", action="store_true",
+                    help="config4 only: prefill every request, then one NVTX range 'prefill' around the last "
+                         "request's prefill and one range 'decode' around a single frame (for ncu --nvtx "
+                         "captures); prints no JSON line")
+    ap.add_argument("--requests", type=int, default=0, help="override the number of requests (config4)")
     return ap.parse_args()
 
 
@@ -434,6 +439,48 @@ def split_requests(reqs, frames: int, world: int):
     return split([r[0].shape[1] + r[2].shape[0] + frames for r in reqs], world)
 
 
+def profile_frame_main(args, wl):
+    """A config-4 engine (requests x 2 rows) for ncu captures: NVTX range
+    'prefill' around the last request's prefill, range 'decode' around one
+    frame after three warm-up frames."""
+    import torch
+
+    from soraku_tts_b200.config import ModelDims
+    from soraku_tts_b200.graph_frame import NativeEngine
+    from soraku_tts_b200.model import SorakuModel
+
+    n = args.requests or wl["requests"]
+    frames = 32
+    reqs = config4_requests(n, wl["text"], wl["ref"])
+    model = SorakuModel.random(ModelDims(), 42, "cuda:0")
+    max_prompt = max(r[0].shape[1] + r[2].shape[0] + 2 for r in reqs)
+    max_len = ((max_prompt + frames + 2 + 63) // 64) * 64
+    eng = NativeEngine(model, max_requests=n, rows_per_request=2, max_len=max_len, max_frames=frames,
+                       max_prefill=max_prompt + 2)
+    for j, (ids, uncond, prompt, seed) in enumerate(reqs):
+        eng.set_sampling(j, cfg=SAMPLING["cfg_scale"], temperature=0.9, temperature_q0=0.9, top_k=50, top_p=0.95,
+                         top_k_q0=50, top_p_q0=0.95, seed=seed, min_new_frames=frames, eos_rule=1)
+        last = j == n - 1
+        if last:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("prefill")
+        eng.prefill(j, ids, uncond, prompt)
+        if last:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
+    eng.capture(n, 1)
+    for _ in range(3):
+        eng.step(True)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("decode")
+    eng.step(True)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print(f"profile frame: {n} requests, {2 * n} rows, {eng.launches_per_step()} kernels per frame", file=sys.stderr)
+    eng.close()
+    return 0
+
+
 def config4_main(args, wl):
     """Batched decode (config 4): every rank decodes its share of the 64
     requests as one batch of 2 rows per request; value = all ranks' frames
@@ -574,6 +621,10 @@ def main():
     args = parse_args()
     wl = WORKLOADS[args.workload]
     if args.workload == "config4" and args.impl != "reference":
+        if args.profile_frame:
+            return profile_frame_main(args, wl)
+        if args.requests:
+            wl = dict(wl, requests=args.requests)
         return config4_main(args, wl)
     if args.impl == "reference":
         return reference_main(args, wl)
