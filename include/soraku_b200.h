@@ -215,6 +215,10 @@ typedef struct {
     int attn_splits;      /* 0 = choose; KV splits per (row, kv head)      */
     int use_pdl;          /* programmatic dependent launch between kernels */
     int l2_prefetch;      /* bulk-prefetch the next kernel's weights       */
+    int gemm_min_rows;    /* batches of at least this many rows run the
+                             tensor-core GEMM path (0 = 5); 1 makes every
+                             batch take it, so a row's arithmetic does not
+                             depend on the batch width                      */
 } skb_engine_opts;
 
 int skb_engine_create(const skb_model_desc *model, const skb_engine_opts *opts, skb_engine **out);
@@ -257,6 +261,19 @@ int skb_engine_read_codes(skb_engine *eng, int request, int first_frame, int n_f
 
 /* Frames decoded so far for a request (host-side counter). */
 int skb_engine_frames(skb_engine *eng, int request);
+
+/* Continuous batching (requests joining and leaving a running batch).
+ * set_rng_stream: the request's Philox stream word (counter = (stream, frame,
+ * q) under its seed; default: the slot index), so a request's draws need not
+ * depend on the slot it occupies.
+ * status: device frame counters and EOS flags of requests [0, n) into host
+ * arrays (synchronises the stream).
+ * move_request: moves request `src`'s decode state (sampling state, codes,
+ * prefix, residual stream, positions, KV pages by page-table exchange) into
+ * slot `dst`, leaving `src` free; for compacting the active slots. */
+int skb_engine_set_rng_stream(skb_engine *eng, int request, uint32_t stream);
+int skb_engine_status(skb_engine *eng, int n, int32_t *frames, int32_t *done, cudaStream_t stream);
+int skb_engine_move_request(skb_engine *eng, int dst, int src, cudaStream_t stream);
 
 /* Device views of engine state for tests: which = 0 x (residual stream)
  * [R, d]; 1 hidden [R, d]; 2 logits [R, V] of the last depth step; 3 pos

@@ -433,6 +433,9 @@ int decode_attn_cluster_width(int groups) {
 }
 
 // C = a.S CTAs per (row, kv head), 1 <= C <= 8; head_dim 128, n_rep <= 2.
+// a.variant 0 picks the double-buffered kernel for more than 32 (row, kv
+// head) groups; a caller whose batch width varies fixes it (1 / 2) so that a
+// row's arithmetic does not depend on how many rows run beside it.
 cudaError_t decode_attn_cluster_launch(const DecodeAttnArgs& a, int R, cudaStream_t s, bool pdl) {
     static bool prepared = false;
     if (!prepared) {
@@ -441,7 +444,7 @@ cudaError_t decode_attn_cluster_launch(const DecodeAttnArgs& a, int R, cudaStrea
         prepared = true;
     }
     if (a.S < 1 || a.S > ATC_MAXC || a.n_rep < 1 || a.n_rep > 2 || a.kv.hd != 128) return cudaErrorInvalidValue;
-    const bool many = R * a.kv.KVH > ATC_MANY_GROUPS;
+    const bool many = a.variant == 0 ? R * a.kv.KVH > ATC_MANY_GROUPS : a.variant == 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.S, a.kv.KVH, R);
     cfg.blockDim = dim3(ATC_THREADS);

@@ -86,6 +86,9 @@ struct skb_engine {
     int graph_active = 0, graph_fpg = 0, graph_pdl = 0;
     int debug = 0;
     float* xn = nullptr;  // batched path: normalised activations [R][max inner size]
+    int gemm_min_rows = 5;  // batches of at least this many rows take the tensor-core GEMM path
+    int attn_variant = 1;   // cluster attention kernel (fixed per engine: see DecodeAttnArgs::variant)
+    int* pt_tmp = nullptr;  // page-table row scratch for move_request
     int frame_nodes = 0;  // kernels of the last built frame
     unsigned long long* kts = nullptr;  // debug kernel timeline [kernels per frame][SKB_KTS_STRIDE]
     std::vector<int> frames_host, pos_host;
@@ -294,6 +297,7 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
             a.H = e->H;
             a.n_rep = e->n_rep;
             a.S = e->S;
+            a.variant = e->attn_variant;
             a.scale = 1.0f / sqrtf((float)e->hd);
             a.out = e->attn;
             a.err = e->err;
@@ -410,13 +414,13 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
     std::vector<Node> nodes;
     // debug timeline: the ring-GEMV frame only (its kernel count is what kts holds)
     auto stamps = [e, &nodes, R]() {
-        return (e->debug && R <= 4) ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr;
+        return (e->debug && R < e->gemm_min_rows) ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr;
     };
     for (const Phase& ph : build_phases(e, n_active)) {
         if (ph.kind == PH_GEMV) {
             GemvArgs g = ph.g;
             g.ts = stamps();
-            if (R > 4)
+            if (R >= e->gemm_min_rows)
                 gemm_rows_nodes(e, ph, R, nodes);
             else
                 nodes.push_back(gemv_node(e, g, R, ph.xm, ph.em));
@@ -575,6 +579,9 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     // head) cluster be resident at once
     e->S = opts->attn_splits > 0 ? opts->attn_splits : decode_attn_cluster_width(e->R * e->KVH);
     if (e->S > 8) e->S = 8;
+    // attention variant by the engine's capacity (the same for every batch width)
+    e->attn_variant = e->R * e->KVH > 32 ? 2 : 1;
+    e->gemm_min_rows = opts->gemm_min_rows > 0 ? opts->gemm_min_rows : 5;
     const size_t n_pages = (size_t)e->R * e->max_pages;
     e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;
     const int qkvd = (e->H + 2 * e->KVH) * e->hd;
@@ -600,7 +607,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->page_table, (size_t)e->R * e->max_pages)
     A(e->err, 8)
     A(e->kts, (size_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5))
-    if (e->R > 4) A(e->xn, (size_t)e->R * 3072)
+    if (e->R >= e->gemm_min_rows) A(e->xn, (size_t)e->R * 3072)
+    A(e->pt_tmp, (size_t)e->max_pages)
     A(e->host_flag, 1)
     A(e->cur_codes, (size_t)e->nreq * e->Q)
     A(e->hist, (size_t)e->nreq * opts->max_frames * e->Q)
@@ -642,7 +650,9 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     e->frames_host.assign(e->nreq, 0);
     e->pos_host.assign(e->R, 0);
     e->st_host.assign(e->nreq, ReqState{});
-    for (auto& s : e->st_host) {
+    for (int r = 0; r < e->nreq; ++r) {
+        ReqState& s = e->st_host[r];
+        s.stream = (unsigned)r;
         s.cfg = 1.5f;
         s.temp = s.temp_q0 = 0.9f;
         s.top_k = s.top_k_q0 = 50;
@@ -961,6 +971,58 @@ int skb_engine_read_codes(skb_engine* e, int req, int first, int n, int64_t* dst
 int skb_engine_frames(skb_engine* e, int req) {
     if (!e || req < 0 || req >= e->nreq) return -1;
     return e->frames_host[req];
+}
+
+int skb_engine_set_rng_stream(skb_engine* e, int req, uint32_t stream) {
+    if (!e || req < 0 || req >= e->nreq) return fail(SKB_ERR_ARG, "set_rng_stream: bad request %d", req);
+    e->st_host[req].stream = stream;
+    const cudaError_t err = cudaMemcpy(reinterpret_cast<char*>(e->st + req) + offsetof(ReqState, stream), &stream,
+                                       sizeof(stream), cudaMemcpyHostToDevice);
+    return err == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "set_rng_stream: %s", cudaGetErrorString(err));
+}
+
+int skb_engine_status(skb_engine* e, int n, int32_t* frames, int32_t* done, cudaStream_t s) {
+    if (!e || n < 0 || n > e->nreq || (n > 0 && (!frames || !done)))
+        return fail(SKB_ERR_ARG, "status: bad arguments");
+    if (n == 0) return SKB_OK;
+    std::vector<ReqState> tmp(n);
+    cudaError_t err = cudaMemcpyAsync(tmp.data(), e->st, sizeof(ReqState) * n, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "status: %s", cudaGetErrorString(err));
+    for (int r = 0; r < n; ++r) {
+        frames[r] = tmp[r].frame;
+        done[r] = tmp[r].done;
+    }
+    return SKB_OK;
+}
+
+int skb_engine_move_request(skb_engine* e, int dst, int src, cudaStream_t s) {
+    if (!e || dst < 0 || dst >= e->nreq || src < 0 || src >= e->nreq)
+        return fail(SKB_ERR_ARG, "move_request: bad slots %d <- %d", dst, src);
+    if (dst == src) return SKB_OK;
+    const size_t D = (size_t)e->D, Q = (size_t)e->Q, MF = (size_t)e->o.max_frames, MP = (size_t)e->max_pages;
+    cudaError_t err = cudaSuccess;
+    auto cp = [&](void* d, const void* sp, size_t bytes) {
+        if (err == cudaSuccess) err = cudaMemcpyAsync(d, sp, bytes, cudaMemcpyDeviceToDevice, s);
+    };
+    cp(e->st + dst, e->st + src, sizeof(ReqState));
+    cp(e->cur_codes + dst * Q, e->cur_codes + src * Q, sizeof(int64_t) * Q);
+    cp(e->hist + dst * MF * Q, e->hist + src * MF * Q, sizeof(int64_t) * MF * Q);
+    cp(e->prefix + dst * D, e->prefix + src * D, sizeof(float) * D);
+    for (int b = 0; b < e->rpr; ++b) {
+        const size_t rd = (size_t)dst * e->rpr + b, rs = (size_t)src * e->rpr + b;
+        cp(e->x + rd * D, e->x + rs * D, sizeof(float) * D);
+        cp(e->pos + rd, e->pos + rs, sizeof(int));
+        // exchange page-table rows: the pages stay unique, the KV stays put
+        cp(e->pt_tmp, e->page_table + rd * MP, sizeof(int) * MP);
+        cp(e->page_table + rd * MP, e->page_table + rs * MP, sizeof(int) * MP);
+        cp(e->page_table + rs * MP, e->pt_tmp, sizeof(int) * MP);
+        e->pos_host[rd] = e->pos_host[rs];
+    }
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "move_request: %s", cudaGetErrorString(err));
+    e->st_host[dst] = e->st_host[src];
+    e->frames_host[dst] = e->frames_host[src];
+    return SKB_OK;
 }
 
 int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {

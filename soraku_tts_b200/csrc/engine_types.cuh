@@ -11,7 +11,7 @@ struct ReqState {
     int top_k, top_k_q0, min_new_frames, eos_rule;
     int frame;  // frames completed (advanced by the q = Q-1 sampler)
     int done;   // q0 drew EOS at least once
-    int pad_;
+    unsigned stream;  // Philox counter word 1: the request's random stream (default: its slot)
     unsigned long long seed;
 };
 
@@ -52,7 +52,7 @@ __device__ __forceinline__ SampleJob depth_sample_job(const DepthSampleArgs& a, 
     J.bos = a.bos;
     J.pad = a.pad;
     J.eos = a.eos;
-    J.u = philox_uniform(st->seed, (uint32_t)r, (uint32_t)frame, (uint32_t)a.q);
+    J.u = philox_uniform(st->seed, st->stream, (uint32_t)frame, (uint32_t)a.q);
     J.ts = a.ts;
     J.pf_rows = a.table + (size_t)a.q * a.V * a.D;
     J.row_floats = a.D;

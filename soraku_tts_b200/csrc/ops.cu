@@ -301,7 +301,7 @@ using namespace skb;
 extern "C" {
 
 const char* skb_last_error(void) { return g_err; }
-int skb_abi_version(void) { return 4; }
+int skb_abi_version(void) { return 5; }
 
 int skb_add_rmsnorm(const float* hidden, const float* prefix, const float* weight, float* out,
                     int B, int D, float eps, cudaStream_t stream) {

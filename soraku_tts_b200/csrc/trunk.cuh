@@ -40,6 +40,7 @@ struct DecodeAttnArgs {
     KVLayout kv;
     int layer;
     int H, n_rep, S;
+    int variant;  // cluster kernel: 0 by rows, 1 single-buffered (few groups), 2 double-buffered
     int nmax;  // score slots per split (dynamic smem n_rep * nmax floats)
     float scale;
     float* part;    // [R][KVH][S][n_rep][hd + 2]

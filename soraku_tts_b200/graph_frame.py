@@ -40,11 +40,11 @@ class NativeEngine:
     """Thin owner of an ``skb_engine*`` (the C ABI of include/soraku_b200.h)."""
 
     def __init__(self, model, *, max_requests=1, rows_per_request=2, max_len=1024, max_frames=1024,
-                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True):
+                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True, gemm_min_rows=0):
         self.model = model
         opts = _lib.skb_engine_opts(max_requests, rows_per_request, max_len, max_frames,
                                     max_prefill if max_prefill else max_len, page_size, attn_splits,
-                                    1 if use_pdl else 0, 1 if l2_prefetch else 0)
+                                    1 if use_pdl else 0, 1 if l2_prefetch else 0, int(gemm_min_rows))
         handle = ctypes.c_void_p()
         desc = model.model_desc()
         _lib.call("skb_engine_create", ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
@@ -100,6 +100,22 @@ class NativeEngine:
 
     def frames(self, request=0) -> int:
         return int(_lib.lib().skb_engine_frames(self.h, request))
+
+    def set_rng_stream(self, request: int, stream: int) -> None:
+        """Philox stream word of a request (counter = (stream, frame, q))."""
+        _lib.call("skb_engine_set_rng_stream", self.h, request, int(stream) & 0xFFFFFFFF)
+
+    def status(self, n: int, stream=None) -> tuple[list[int], list[int]]:
+        """Device frame counters and EOS flags of requests [0, n)."""
+        frames = (ctypes.c_int32 * max(n, 1))()
+        done = (ctypes.c_int32 * max(n, 1))()
+        _lib.call("skb_engine_status", self.h, n, ctypes.addressof(frames), ctypes.addressof(done),
+                  _lib.stream_ptr(stream))
+        return list(frames[:n]), list(done[:n])
+
+    def move_request(self, dst: int, src: int, stream=None) -> None:
+        """Move request ``src``'s decode state into slot ``dst`` (slot compaction)."""
+        _lib.call("skb_engine_move_request", self.h, dst, src, _lib.stream_ptr(stream))
 
     def read_codes(self, request, first, n, out=None, stream=None, sync=True) -> torch.Tensor:
         """Codes [n, Q] of frames first..first+n-1.  The copy is asynchronous on

@@ -75,7 +75,7 @@ int main(void) {
 
 
 def test_abi_version_and_error_string_without_gpu(lib):
-    assert lib.lib().skb_abi_version() == 4
+    assert lib.lib().skb_abi_version() == 5
     assert isinstance(lib.last_error(), str)
     # argument validation happens before any CUDA call: a bad call fails cleanly on CPU
     st = lib.lib().skb_swiglu_gemv(None, None, None, None, 2, 2048, 1022, None)

@@ -1,0 +1,158 @@
+"""Continuous-batching scheduler logic on CPU, against a fake engine with the
+NativeEngine surface: admission into free slots, slot compaction, per-request
+stop on EOS (from min_new_frames on, frame not emitted) or frame budget,
+per-frame streaming, capacity checks and independence of the slot a request
+runs in (its random stream is fixed, not its slot)."""
+
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from soraku_tts_b200.scheduler import ContinuousBatcher, DecodeRequest
+
+Q, EOS = 16, 2049
+
+
+def code(seed: int, stream: int, frame: int, q: int) -> int:
+    """The fake engine's draw: a hash of (seed, stream, frame, q); q0 of a
+    frame listed in the seed's EOS frames is EOS when allowed."""
+    h = (seed * 1000003 + stream * 7919 + frame * 104729 + q * 31) & 0x7FFFFFFF
+    return h % 2048
+
+
+class FakeEngine:
+    def __init__(self, *, max_requests, rows_per_request, max_len, max_frames, max_prefill, eos_frames=None, **kw):
+        self.n = max_requests
+        self.max_frames = max_frames
+        self.max_len = max_len
+        self.eos_frames = eos_frames or {}
+        self.st = [dict(seed=0, min=0, frame=0, done=0, stream=i, pos=0) for i in range(max_requests)]
+        self.hist = np.zeros((max_requests, max_frames, Q), np.int64)
+        self.graph = None
+        self.kw = kw
+        self.log = []
+
+    def set_sampling(self, j, *, seed, min_new_frames, eos_rule, **kw):
+        assert eos_rule == 1
+        self.st[j].update(seed=seed, min=min_new_frames)
+
+    def set_rng_stream(self, j, stream):
+        self.st[j]["stream"] = stream
+
+    def prefill(self, j, ids, uncond, prompt, speaker):
+        n_prompt = 0 if prompt is None else torch.as_tensor(prompt).numel() // Q
+        self.st[j].update(frame=0, done=0, pos=torch.as_tensor(ids).shape[1] + 1 + n_prompt)
+        self.log.append(("prefill", j))
+
+    def capture(self, n, fpg):
+        self.graph = (n, fpg)
+        self.log.append(("capture", n, fpg))
+
+    def step(self, mask_eos_q0=True):
+        n, fpg = self.graph
+        for j in range(n):
+            s = self.st[j]
+            for _ in range(fpg):
+                f = s["frame"]
+                assert f < self.max_frames and s["pos"] < self.max_len, "capacity exceeded"
+                row = [code(s["seed"], s["stream"], f, q) for q in range(Q)]
+                if f >= s["min"] and f in self.eos_frames.get(s["seed"], ()):
+                    row[0] = EOS
+                    s["done"] = 1
+                self.hist[j, f] = row
+                s["frame"] += 1
+                s["pos"] += 1
+
+    def status(self, n):
+        return [s["frame"] for s in self.st[:n]], [s["done"] for s in self.st[:n]]
+
+    def read_codes(self, j, first, n):
+        return torch.from_numpy(self.hist[j, first:first + n].copy())
+
+    def move_request(self, dst, src):
+        self.st[dst] = dict(self.st[src])
+        self.hist[dst] = self.hist[src]
+        self.log.append(("move", dst, src))
+
+    def close(self):
+        pass
+
+
+def make(slots=3, fpg=2, eos_frames=None, max_frames=64, max_len=256):
+    model = SimpleNamespace(config=SimpleNamespace(num_codebooks=Q, audio_eos_id=EOS))
+    eng = {}
+
+    def factory(**kw):
+        eng["e"] = FakeEngine(eos_frames=eos_frames, **kw)
+        return eng["e"]
+
+    b = ContinuousBatcher(model, slots=slots, max_len=max_len, max_frames=max_frames, frames_per_graph=fpg,
+                          engine_factory=factory)
+    return b, eng["e"]
+
+
+def expected(seed, max_new, min_new, eos_frames):
+    rows = []
+    for f in range(max_new):
+        if f >= min_new and f in eos_frames.get(seed, ()):
+            return np.array(rows, np.int64).reshape(-1, Q), "eos"
+        rows.append([code(seed, 0, f, q) for q in range(Q)])
+    return np.array(rows, np.int64).reshape(-1, Q), "max_frames"
+
+
+def test_ragged_requests_join_and_leave_with_compaction():
+    eos_frames = {105: {3}, 107: {1, 6}, 108: {0}}  # 107: EOS at 1 is masked by min_new_frames=2
+    b, e = make(slots=3, fpg=2, eos_frames=eos_frames)
+    budgets = [5, 9, 2, 7, 1, 4, 8, 3, 0]
+    mins = [0, 0, 0, 0, 0, 2, 2, 0, 0]
+    streamed = {}
+    for i, (m, mn) in enumerate(zip(budgets, mins)):
+        b.submit(DecodeRequest(rid=f"r{i}", input_ids=np.full((1, 3 + i), 7, np.int64),
+                               prompt_codes=np.zeros((2 + i, Q), np.int64), max_new_frames=m, min_new_frames=mn,
+                               seed=100 + i, on_frame=lambda rid, c: streamed.setdefault(rid, []).append(c)))
+    out = b.run()
+    assert sorted(out) == sorted(f"r{i}" for i in range(len(budgets)))
+    for i, (m, mn) in enumerate(zip(budgets, mins)):
+        want, why = expected(100 + i, m, mn, eos_frames)
+        got = out[f"r{i}"]
+        np.testing.assert_array_equal(got, want)
+        assert b.stop_reason[f"r{i}"] == why
+        if len(want):
+            np.testing.assert_array_equal(np.stack(streamed[f"r{i}"]), want)
+        else:
+            assert f"r{i}" not in streamed
+    assert b.stats["moves"] > 0  # a finished slot below an active one was compacted
+    assert b.active() == 0 and b.pending() == 0
+    # the graph always covered a contiguous prefix of the slots
+    assert all(n <= 3 for kind, *rest in e.log if kind == "capture" for n in rest[:1])
+
+
+def test_slot_does_not_change_a_request():
+    """The same request decoded alone and inside a busy batch: same codes."""
+    alone, _ = make(slots=1, fpg=3)
+    alone.submit(DecodeRequest(rid="x", input_ids=np.ones((1, 4), np.int64), max_new_frames=10, seed=42))
+    a = alone.run()["x"]
+    busy, _ = make(slots=4, fpg=3)
+    for i in range(5):
+        busy.submit(DecodeRequest(rid=i, input_ids=np.ones((1, 4), np.int64), max_new_frames=2 + i, seed=i))
+    busy.submit(DecodeRequest(rid="x", input_ids=np.ones((1, 4), np.int64), max_new_frames=10, seed=42))
+    np.testing.assert_array_equal(busy.run()["x"], a)
+
+
+def test_capacity_and_duplicate_checks():
+    b, _ = make(slots=2, fpg=4, max_frames=16, max_len=64)
+    with pytest.raises(ValueError):
+        b.submit(DecodeRequest(rid=0, input_ids=np.ones((1, 4), np.int64), max_new_frames=13))  # 13 + 4 > 16
+    with pytest.raises(ValueError):
+        b.submit(DecodeRequest(rid=1, input_ids=np.ones((1, 50), np.int64), max_new_frames=10))  # 51 + 10 + 4 > 64
+    with pytest.raises(ValueError):
+        b.submit(DecodeRequest(rid=2, input_ids=np.ones((4,), np.int64)))  # not [1, L]
+    b.submit(DecodeRequest(rid=3, input_ids=np.ones((1, 4), np.int64), max_new_frames=12))
+    with pytest.raises(ValueError):
+        b.submit(DecodeRequest(rid=3, input_ids=np.ones((1, 4), np.int64), max_new_frames=2))
+    out = b.run()
+    assert out[3].shape == (12, Q)
