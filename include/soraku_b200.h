@@ -219,6 +219,11 @@ typedef struct {
                              tensor-core GEMM path (0 = 5); 1 makes every
                              batch take it, so a row's arithmetic does not
                              depend on the batch width                      */
+    int kv_pages;         /* 0: every row owns ceil(max_len / page_size)
+                             pages; > 0: a shared pool of this many pages
+                             per layer, mapped to rows by
+                             skb_engine_map_pages (unmapped positions are
+                             refused by prefill and step)                   */
 } skb_engine_opts;
 
 int skb_engine_create(const skb_model_desc *model, const skb_engine_opts *opts, skb_engine **out);
@@ -274,6 +279,11 @@ int skb_engine_frames(skb_engine *eng, int request);
 int skb_engine_set_rng_stream(skb_engine *eng, int request, uint32_t stream);
 int skb_engine_status(skb_engine *eng, int n, int32_t *frames, int32_t *done, cudaStream_t stream);
 int skb_engine_move_request(skb_engine *eng, int dst, int src, cudaStream_t stream);
+/* Shared KV pool (opts.kv_pages > 0): row `row`'s logical pages [first,
+ * first + n) become pool pages pages[0..n) (host int32; -1 unmaps).  A
+ * page must not be mapped to two rows at once; the caller owns the free
+ * list (soraku_tts_b200/scheduler.py PagePool). */
+int skb_engine_map_pages(skb_engine *eng, int row, int first, int n, const int32_t *pages);
 
 /* Device views of engine state for tests: which = 0 x (residual stream)
  * [R, d]; 1 hidden [R, d]; 2 logits [R, V] of the last depth step; 3 pos

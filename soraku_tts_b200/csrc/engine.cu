@@ -89,6 +89,9 @@ struct skb_engine {
     int gemm_min_rows = 5;  // batches of at least this many rows take the tensor-core GEMM path
     int attn_variant = 1;   // cluster attention kernel (fixed per engine: see DecodeAttnArgs::variant)
     int* pt_tmp = nullptr;  // page-table row scratch for move_request
+    int pool_pages = 0;     // KV pages per layer
+    bool shared_pool = false;  // pages mapped by the caller (skb_engine_map_pages)
+    std::vector<int> pt_host;  // host mirror of the page table
     int frame_nodes = 0;  // kernels of the last built frame
     unsigned long long* kts = nullptr;  // debug kernel timeline [kernels per frame][SKB_KTS_STRIDE]
     std::vector<int> frames_host, pos_host;
@@ -135,7 +138,7 @@ KVLayout kv_layout(const skb_engine* e) {
     k.KVH = e->KVH;
     k.hd = e->hd;
     k.layer_floats = e->layer_floats;
-    k.n_pages = e->R * e->max_pages;
+    k.n_pages = e->pool_pages;
     return k;
 }
 
@@ -582,7 +585,9 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     // attention variant by the engine's capacity (the same for every batch width)
     e->attn_variant = e->R * e->KVH > 32 ? 2 : 1;
     e->gemm_min_rows = opts->gemm_min_rows > 0 ? opts->gemm_min_rows : 5;
-    const size_t n_pages = (size_t)e->R * e->max_pages;
+    e->shared_pool = opts->kv_pages > 0;
+    e->pool_pages = e->shared_pool ? opts->kv_pages : e->R * e->max_pages;
+    const size_t n_pages = (size_t)e->pool_pages;
     e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;
     const int qkvd = (e->H + 2 * e->KVH) * e->hd;
     const int actd = e->F > e->I ? e->F : e->I;
@@ -642,10 +647,11 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
         cudaMemcpy(e->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(e->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
     }
-    {  // identity page table: row r owns pages [r*max_pages, (r+1)*max_pages)
-        std::vector<int> pt((size_t)e->R * e->max_pages);
-        for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
-        cudaMemcpy(e->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice);
+    {  // own pages: row r holds [r*max_pages, (r+1)*max_pages); shared pool: unmapped
+        e->pt_host.assign((size_t)e->R * e->max_pages, -1);
+        if (!e->shared_pool)
+            for (size_t i = 0; i < e->pt_host.size(); ++i) e->pt_host[i] = (int)i;
+        cudaMemcpy(e->page_table, e->pt_host.data(), e->pt_host.size() * 4, cudaMemcpyHostToDevice);
     }
     e->frames_host.assign(e->nreq, 0);
     e->pos_host.assign(e->R, 0);
@@ -686,6 +692,17 @@ int skb_engine_destroy(skb_engine* e) {
     if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
     for (void* p : e->allocs) cudaFree(p);
     delete e;
+    return SKB_OK;
+}
+
+// Shared pool: the row's positions [0, n) must sit on mapped pages.
+static int check_pages(const skb_engine* e, int row, int n) {
+    if (!e->shared_pool) return SKB_OK;
+    const int need = (n + e->o.page_size - 1) >> e->page_log2;
+    for (int p = 0; p < need && p < e->max_pages; ++p)
+        if (e->pt_host[(size_t)row * e->max_pages + p] < 0)
+            return fail(SKB_ERR_CAPACITY, "row %d: KV page %d (positions %d..) is not mapped", row, p,
+                        p * e->o.page_size);
     return SKB_OK;
 }
 
@@ -757,6 +774,8 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         if (p > e->o.max_prefill || p >= e->o.max_len)
             return fail(SKB_ERR_CAPACITY, "prefill %d exceeds max_prefill=%d / max_len=%d", p, e->o.max_prefill,
                         e->o.max_len);
+        const int pst = check_pages(e, row, p);
+        if (pst) return pst;
     }
     const int T = (int)toks.size();
     std::vector<int64_t> frames((size_t)(n_prompt + 1) * e->Q);
@@ -912,6 +931,11 @@ int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream
 
 static int check_capacity(skb_engine* e, int n_active, int frames) {
     for (int r = 0; r < n_active; ++r) {
+        for (int b = 0; b < e->rpr; ++b) {
+            const int row = r * e->rpr + b;
+            const int st = check_pages(e, row, e->pos_host[row] + frames);
+            if (st) return st;
+        }
         if (e->frames_host[r] + frames > e->o.max_frames)
             return fail(SKB_ERR_CAPACITY, "frame buffer full (%d + %d > max_frames %d)", e->frames_host[r], frames,
                         e->o.max_frames);
@@ -973,6 +997,21 @@ int skb_engine_frames(skb_engine* e, int req) {
     return e->frames_host[req];
 }
 
+int skb_engine_map_pages(skb_engine* e, int row, int first, int n, const int32_t* pages) {
+    if (!e || row < 0 || row >= e->R || first < 0 || n < 0 || first + n > e->max_pages || (n > 0 && !pages))
+        return fail(SKB_ERR_ARG, "map_pages: bad arguments (row %d, pages [%d, %d))", row, first, first + n);
+    if (!e->shared_pool) return fail(SKB_ERR_STATE, "map_pages: the engine was created without a shared KV pool");
+    for (int i = 0; i < n; ++i)
+        if (pages[i] < -1 || pages[i] >= e->pool_pages)
+            return fail(SKB_ERR_ARG, "map_pages: page %d outside the pool of %d", pages[i], e->pool_pages);
+    if (n == 0) return SKB_OK;
+    const cudaError_t err = cudaMemcpy(e->page_table + (size_t)row * e->max_pages + first, pages, sizeof(int) * n,
+                                       cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "map_pages: %s", cudaGetErrorString(err));
+    for (int i = 0; i < n; ++i) e->pt_host[(size_t)row * e->max_pages + first + i] = pages[i];
+    return SKB_OK;
+}
+
 int skb_engine_set_rng_stream(skb_engine* e, int req, uint32_t stream) {
     if (!e || req < 0 || req >= e->nreq) return fail(SKB_ERR_ARG, "set_rng_stream: bad request %d", req);
     e->st_host[req].stream = stream;
@@ -1017,6 +1056,7 @@ int skb_engine_move_request(skb_engine* e, int dst, int src, cudaStream_t s) {
         cp(e->pt_tmp, e->page_table + rd * MP, sizeof(int) * MP);
         cp(e->page_table + rd * MP, e->page_table + rs * MP, sizeof(int) * MP);
         cp(e->page_table + rs * MP, e->pt_tmp, sizeof(int) * MP);
+        for (size_t p = 0; p < MP; ++p) std::swap(e->pt_host[rd * MP + p], e->pt_host[rs * MP + p]);
         e->pos_host[rd] = e->pos_host[rs];
     }
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "move_request: %s", cudaGetErrorString(err));

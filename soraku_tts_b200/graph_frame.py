@@ -40,11 +40,14 @@ class NativeEngine:
     """Thin owner of an ``skb_engine*`` (the C ABI of include/soraku_b200.h)."""
 
     def __init__(self, model, *, max_requests=1, rows_per_request=2, max_len=1024, max_frames=1024,
-                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True, gemm_min_rows=0):
+                 max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True, gemm_min_rows=0,
+                 kv_pages=0):
         self.model = model
         opts = _lib.skb_engine_opts(max_requests, rows_per_request, max_len, max_frames,
                                     max_prefill if max_prefill else max_len, page_size, attn_splits,
-                                    1 if use_pdl else 0, 1 if l2_prefetch else 0, int(gemm_min_rows))
+                                    1 if use_pdl else 0, 1 if l2_prefetch else 0, int(gemm_min_rows),
+                                    int(kv_pages))
+        self.page_size = page_size
         handle = ctypes.c_void_p()
         desc = model.model_desc()
         _lib.call("skb_engine_create", ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
@@ -112,6 +115,12 @@ class NativeEngine:
         _lib.call("skb_engine_status", self.h, n, ctypes.addressof(frames), ctypes.addressof(done),
                   _lib.stream_ptr(stream))
         return list(frames[:n]), list(done[:n])
+
+    def map_pages(self, row: int, first: int, pages) -> None:
+        """Shared KV pool: logical pages [first, first + len(pages)) of a row
+        become these pool pages (-1 unmaps)."""
+        arr = (ctypes.c_int32 * max(len(pages), 1))(*[int(p) for p in pages])
+        _lib.call("skb_engine_map_pages", self.h, row, first, len(pages), ctypes.addressof(arr))
 
     def move_request(self, dst: int, src: int, stream=None) -> None:
         """Move request ``src``'s decode state into slot ``dst`` (slot compaction)."""

@@ -11,7 +11,10 @@ budget is spent -- without stopping the others.  Finished slots are
 compacted (the highest active request moves into the hole: its sampling
 state, codes, residual stream and positions are copied, its KV pages change
 hands by a page-table exchange), so the captured graph always covers a
-contiguous prefix of the slots.
+contiguous prefix of the slots.  With ``kv_pages`` the KV cache is one shared
+pool of pages: a request is admitted when the pool holds the pages its
+prompt and frame budget need (both CFG rows), which it keeps until it
+finishes, so short requests do not reserve a full ``max_len`` per row.
 
 Determinism: every request draws from its own Philox stream (counter =
 (stream 0, frame, q) under the request's seed), the engine runs the
@@ -65,6 +68,27 @@ class _Slot:
     req: DecodeRequest
     emitted: int = 0
     frames: list = field(default_factory=list)
+    pages: list = field(default_factory=list)  # shared pool: per CFG row, its pool pages in order
+
+
+class PagePool:
+    """Free list of a shared KV pool's pages (ids 0..n-1, lowest first)."""
+
+    def __init__(self, n_pages: int):
+        self.n = int(n_pages)
+        self._free = list(range(self.n - 1, -1, -1))
+
+    def available(self) -> int:
+        return len(self._free)
+
+    def take(self, k: int) -> list[int]:
+        if k > len(self._free):
+            raise RuntimeError(f"KV pool exhausted: {k} pages wanted, {len(self._free)} free")
+        return [self._free.pop() for _ in range(k)]
+
+    def give(self, pages) -> None:
+        self._free.extend(sorted(pages, reverse=True))
+        self._free.sort(reverse=True)
 
 
 class ContinuousBatcher:
@@ -72,7 +96,8 @@ class ContinuousBatcher:
     request slots (2 CFG rows each)."""
 
     def __init__(self, model, *, slots: int, max_len: int, max_frames: int, frames_per_graph: int = 4,
-                 max_prefill: int | None = None, device: Any = "cuda", engine_factory=None, **engine_kw):
+                 max_prefill: int | None = None, kv_pages: int | None = None, page_size: int = 64,
+                 device: Any = "cuda", engine_factory=None, **engine_kw):
         self.model = as_soraku_model(model, torch.device(device)) if engine_factory is None else model
         cfg = self.model.config
         self.Q = int(cfg.num_codebooks)
@@ -88,8 +113,14 @@ class ContinuousBatcher:
         # (row, kv head): a row's arithmetic is the same at every width
         kw = dict(gemm_min_rows=1, attn_splits=1)
         kw.update(engine_kw)
+        self.page_size = int(page_size)
+        self.max_pages = -(-self.max_len // self.page_size)
+        self.pool = PagePool(kv_pages) if kv_pages else None
+        if kv_pages:
+            kw["kv_pages"] = int(kv_pages)
         self.engine = make(max_requests=slots, rows_per_request=2, max_len=self.max_len,
-                           max_frames=self.max_frames, max_prefill=self.max_prefill, **kw)
+                           max_frames=self.max_frames, max_prefill=self.max_prefill, page_size=self.page_size,
+                           **kw)
         self.slots: list[_Slot | None] = [None] * slots
         self.queue: deque[DecodeRequest] = deque()
         self.results: dict[Hashable, np.ndarray] = {}
@@ -120,6 +151,9 @@ class ContinuousBatcher:
         if req.max_new_frames + self.fpg > self.max_frames:
             raise ValueError(f"request {req.rid!r}: {req.max_new_frames} frames exceed max_frames "
                              f"{self.max_frames}")
+        if self.pool is not None and sum(self._pages_needed(req)) > self.pool.n:
+            raise ValueError(f"request {req.rid!r} needs {sum(self._pages_needed(req))} KV pages, the pool has "
+                             f"{self.pool.n}")
         if req.rid in self.results or any(s is not None and s.req.rid == req.rid for s in self.slots) or \
                 any(q.rid == req.rid for q in self.queue):
             raise ValueError(f"request id {req.rid!r} already submitted")
@@ -161,6 +195,16 @@ class ContinuousBatcher:
         self.engine.close()
 
     # ------------------------------------------------------------ internals
+    def _pages_needed(self, req: DecodeRequest) -> tuple[int, int]:
+        """Pages of the cond and uncond rows for the prompt, the frame budget
+        and one chunk of overrun."""
+        slot = 1 if req.speaker is not None and getattr(self.model.config, "speaker_condition_mode", "") == "slot" \
+            else 0
+        n_prompt = 0 if req.prompt_codes is None else int(torch.as_tensor(req.prompt_codes).numel() // self.Q)
+        tail = slot + 1 + n_prompt + req.max_new_frames + self.fpg
+        lens = (torch.as_tensor(req.input_ids).shape[-1] + tail, self._uncond(req).numel() + tail)
+        return tuple(-(-n // self.page_size) for n in lens)
+
     def _uncond(self, req: DecodeRequest) -> torch.Tensor:
         if req.uncond_ids is None:
             return torch.tensor([[UNCOND_TEXT_ID]], dtype=torch.int64)
@@ -175,7 +219,7 @@ class ContinuousBatcher:
                 hi -= 1
             if lo >= hi:
                 return
-            self.engine.move_request(lo, hi)
+            self.engine.move_request(lo, hi)  # also exchanges the two slots' page-table rows
             self.slots[lo], self.slots[hi] = self.slots[hi], None
             self.stats["moves"] += 1
 
@@ -191,13 +235,23 @@ class ContinuousBatcher:
                 self.stop_reason[req.rid] = "max_frames"
                 continue
             e = self.engine
+            pages = []
+            if self.pool is not None:
+                need = self._pages_needed(req)
+                if sum(need) > self.pool.available():  # wait for pages, keeping arrival order
+                    self.queue.appendleft(req)
+                    return
+                for b, k in enumerate(need):
+                    got = self.pool.take(k)
+                    e.map_pages(2 * j + b, 0, got + [-1] * (self.max_pages - k))
+                    pages.append(got)
             e.set_sampling(j, cfg=req.cfg_scale, temperature=req.temperature,
                            temperature_q0=req.temperature if req.temperature_q0 is None else req.temperature_q0,
                            top_k=req.top_k, top_p=req.top_p, top_k_q0=req.top_k, top_p_q0=req.top_p,
                            seed=req.seed, min_new_frames=req.min_new_frames, eos_rule=1)
             e.set_rng_stream(j, 0)
             e.prefill(j, req.input_ids, self._uncond(req), req.prompt_codes, req.speaker)
-            self.slots[j] = _Slot(req)
+            self.slots[j] = _Slot(req, pages=pages)
             self.stats["admitted"] += 1
 
     def _collect(self, j: int, frames: int) -> None:
@@ -222,4 +276,8 @@ class ContinuousBatcher:
         if stop is not None:
             self.results[req.rid] = (np.stack(s.frames) if s.frames else np.zeros((0, self.Q), np.int64))
             self.stop_reason[req.rid] = stop
+            if self.pool is not None:
+                for b, pages in enumerate(s.pages):  # back to the pool; the rows map nothing
+                    self.engine.map_pages(2 * j + b, 0, [-1] * self.max_pages)
+                    self.pool.give(pages)
             self.slots[j] = None

@@ -25,10 +25,16 @@ def code(seed: int, stream: int, frame: int, q: int) -> int:
 
 
 class FakeEngine:
-    def __init__(self, *, max_requests, rows_per_request, max_len, max_frames, max_prefill, eos_frames=None, **kw):
+    def __init__(self, *, max_requests, rows_per_request, max_len, max_frames, max_prefill, eos_frames=None,
+                 page_size=64, kv_pages=0, **kw):
         self.n = max_requests
         self.max_frames = max_frames
         self.max_len = max_len
+        self.page_size = page_size
+        self.max_pages = -(-max_len // page_size)
+        self.shared = kv_pages > 0
+        own = [[r * self.max_pages + p for p in range(self.max_pages)] for r in range(2 * max_requests)]
+        self.pt = [[-1] * self.max_pages for _ in range(2 * max_requests)] if self.shared else own
         self.eos_frames = eos_frames or {}
         self.st = [dict(seed=0, min=0, frame=0, done=0, stream=i, pos=0) for i in range(max_requests)]
         self.hist = np.zeros((max_requests, max_frames, Q), np.int64)
@@ -43,9 +49,25 @@ class FakeEngine:
     def set_rng_stream(self, j, stream):
         self.st[j]["stream"] = stream
 
+    def map_pages(self, row, first, pages):
+        assert self.shared
+        self.pt[row][first:first + len(pages)] = list(pages)
+
+    def _check_pages(self, row, n):
+        need = -(-n // self.page_size)
+        assert all(p >= 0 for p in self.pt[row][:need]), f"row {row}: positions < {n} not mapped"
+
+    def _check_unique(self, n_active):
+        used = [p for row in self.pt[:2 * n_active] for p in row if p >= 0]
+        assert len(used) == len(set(used)), "a page is mapped to two rows"
+
     def prefill(self, j, ids, uncond, prompt, speaker):
         n_prompt = 0 if prompt is None else torch.as_tensor(prompt).numel() // Q
-        self.st[j].update(frame=0, done=0, pos=torch.as_tensor(ids).shape[1] + 1 + n_prompt)
+        lc = torch.as_tensor(ids).shape[1] + 1 + n_prompt
+        lu = torch.as_tensor(uncond).numel() + 1 + n_prompt
+        self._check_pages(2 * j, lc)
+        self._check_pages(2 * j + 1, lu)
+        self.st[j].update(frame=0, done=0, pos=lc, upos=lu)
         self.log.append(("prefill", j))
 
     def capture(self, n, fpg):
@@ -54,8 +76,11 @@ class FakeEngine:
 
     def step(self, mask_eos_q0=True):
         n, fpg = self.graph
+        self._check_unique(n)
         for j in range(n):
             s = self.st[j]
+            self._check_pages(2 * j, s["pos"] + fpg)
+            self._check_pages(2 * j + 1, s["upos"] + fpg)
             for _ in range(fpg):
                 f = s["frame"]
                 assert f < self.max_frames and s["pos"] < self.max_len, "capacity exceeded"
@@ -66,6 +91,7 @@ class FakeEngine:
                 self.hist[j, f] = row
                 s["frame"] += 1
                 s["pos"] += 1
+                s["upos"] += 1
 
     def status(self, n):
         return [s["frame"] for s in self.st[:n]], [s["done"] for s in self.st[:n]]
@@ -76,13 +102,15 @@ class FakeEngine:
     def move_request(self, dst, src):
         self.st[dst] = dict(self.st[src])
         self.hist[dst] = self.hist[src]
+        for b in range(2):
+            self.pt[2 * dst + b], self.pt[2 * src + b] = self.pt[2 * src + b], self.pt[2 * dst + b]
         self.log.append(("move", dst, src))
 
     def close(self):
         pass
 
 
-def make(slots=3, fpg=2, eos_frames=None, max_frames=64, max_len=256):
+def make(slots=3, fpg=2, eos_frames=None, max_frames=64, max_len=256, kv_pages=None, page_size=64):
     model = SimpleNamespace(config=SimpleNamespace(num_codebooks=Q, audio_eos_id=EOS))
     eng = {}
 
@@ -91,7 +119,7 @@ def make(slots=3, fpg=2, eos_frames=None, max_frames=64, max_len=256):
         return eng["e"]
 
     b = ContinuousBatcher(model, slots=slots, max_len=max_len, max_frames=max_frames, frames_per_graph=fpg,
-                          engine_factory=factory)
+                          kv_pages=kv_pages, page_size=page_size, engine_factory=factory)
     return b, eng["e"]
 
 
@@ -156,3 +184,28 @@ def test_capacity_and_duplicate_checks():
         b.submit(DecodeRequest(rid=3, input_ids=np.ones((1, 4), np.int64), max_new_frames=2))
     out = b.run()
     assert out[3].shape == (12, Q)
+
+
+def test_shared_kv_pool_admits_by_free_pages():
+    """A pool too small for every slot's full reservation: requests wait for
+    pages in arrival order, no page is ever mapped to two rows, every page
+    returns to the pool, and the codes are those of the own-pages engine."""
+    reqs = [(i, 3 + 5 * (i % 3), 4 + 3 * (i % 4)) for i in range(8)]  # (rid, text length, frames)
+
+    def submit_all(b):
+        for rid, L, m in reqs:
+            b.submit(DecodeRequest(rid=rid, input_ids=np.ones((1, L), np.int64),
+                                   prompt_codes=np.zeros((6, Q), np.int64), max_new_frames=m, seed=rid))
+
+    own, _ = make(slots=4, fpg=2, max_len=128, page_size=8)
+    submit_all(own)
+    want = own.run()
+    pooled, e = make(slots=4, fpg=2, max_len=128, page_size=8, kv_pages=14)
+    submit_all(pooled)
+    got = pooled.run()
+    for rid, _, _ in reqs:
+        np.testing.assert_array_equal(got[rid], want[rid])
+    assert pooled.pool.available() == 14
+    assert all(p == -1 for row in e.pt for p in row)
+    with pytest.raises(ValueError):  # can never fit the pool
+        pooled.submit(DecodeRequest(rid="big", input_ids=np.ones((1, 60), np.int64), max_new_frames=50))

@@ -71,14 +71,18 @@ def _static(model, reqs):
     return out
 
 
-def test_continuous_batching_equals_static_batch(small):
+@pytest.mark.parametrize("kv_pages", [None, 9])
+def test_continuous_batching_equals_static_batch(small, kv_pages):
+    """kv_pages 9: a shared KV pool of 9 pages of 16 positions (a request
+    needs 3-4), so admission also waits for free pages."""
     from soraku_tts_b200.scheduler import ContinuousBatcher, DecodeRequest
 
     data, model = small
     reqs = _requests(data)
     want = _static(model, reqs)
     streamed = {}
-    b = ContinuousBatcher(model, slots=3, max_len=512, max_frames=64, frames_per_graph=2)
+    b = ContinuousBatcher(model, slots=3, max_len=512, max_frames=64, frames_per_graph=2, kv_pages=kv_pages,
+                          page_size=16 if kv_pages else 64)
     for r in reqs:
         b.submit(DecodeRequest(**r, on_frame=lambda rid, c: streamed.setdefault(rid, []).append(c)))
     got = b.run()
@@ -89,4 +93,6 @@ def test_continuous_batching_equals_static_batch(small):
         np.testing.assert_array_equal(got[r["rid"]], want[r["rid"]], err_msg=f"request {r['rid']}")
         if len(want[r["rid"]]):
             np.testing.assert_array_equal(np.stack(streamed[r["rid"]]), want[r["rid"]])
+    if kv_pages:
+        assert b.pool.available() == kv_pages
     b.close()
