@@ -54,8 +54,6 @@ __device__ __forceinline__ SampleJob depth_sample_job(const DepthSampleArgs& a, 
     J.eos = a.eos;
     J.u = philox_uniform(st->seed, st->stream, (uint32_t)frame, (uint32_t)a.q);
     J.ts = a.ts;
-    J.pf_rows = a.table + (size_t)a.q * a.V * a.D;
-    J.row_floats = a.D;
     *frame_out = frame;
     return J;
 }

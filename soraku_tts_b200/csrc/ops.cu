@@ -225,8 +225,6 @@ __global__ void __launch_bounds__(SAMPLER_THREADS) cfg_sample_kernel(
     J.eos = eos;
     J.u = philox_uniform(p.seed, p.request, p.frame, p.q);
     J.ts = nullptr;
-    J.pf_rows = nullptr;
-    J.row_floats = 0;
     const int code = sample_one(J, smem);
     if (threadIdx.x == 0) {
         codes_out[r] = code;

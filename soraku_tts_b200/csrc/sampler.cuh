@@ -117,11 +117,6 @@ struct SampleJob {
     int top_k, mask_eos, bos, pad, eos;
     float u;
     unsigned long long* ts;  // optional debug stage stamps (slots 6..11 of a kernel timeline)
-    // optional: rows of `row_floats` floats indexed by code, of which the
-    // candidates' rows are prefetched into L2 once the top-k set is known
-    // (the caller reads the drawn code's row right after the draw)
-    const float* pf_rows;
-    int row_floats;
 };
 
 // Block-wide exclusive scan of one int per thread (256 threads).
@@ -346,10 +341,6 @@ static __device__ int sample_one(const SampleJob& J, unsigned char* smem, int* n
         }
         Sync::sync();
         n = sc[10];
-    }
-    if (J.pf_rows != nullptr && tid < n && tid < 64) {
-        const uint32_t idx = 0xffffffffu - (uint32_t)(sorted[tid] & 0xffffffffull);
-        bulk_prefetch_l2(J.pf_rows + (size_t)idx * J.row_floats, (unsigned)J.row_floats * 4u);
     }
     // e_j, zero-padded to a multiple of 32 (adding +0 to a running sum of
     // non-negative terms changes nothing, so the sequential passes below run
