@@ -220,11 +220,15 @@ __global__ void __launch_bounds__(256) prefill_qk_kernel(const float* __restrict
     }
 }
 
-// Causal attention of a row's prompt: grid (ceil(L/32), KVH, n_rows); each
-// CTA serves 32 query positions x n_rep heads = 64 query vectors (8 per warp,
-// staged pre-scaled in shared memory); keys and values stream through shared
-// memory 32 positions at a time with an online softmax.
-constexpr int PATTN_SMEM = (64 * 128 + 32 * 129 + 32 * 128) * 4;
+// Causal attention of a row's prompt: grid (ceil(L/16), KVH, n_rows); each
+// CTA serves 16 query positions x n_rep heads (<= 32 query vectors, 4 per
+// warp, staged pre-scaled in shared memory); keys and values stream through
+// shared memory 32 positions at a time with an online softmax.  The CTA of
+// the last query block walks every key block, so the query block is kept
+// small: that CTA's serial chain sets the kernel's time.
+constexpr int PATTN_QP = 16;                // query positions per CTA
+constexpr int PATTN_QVEC = 2 * PATTN_QP;    // query vectors per CTA (n_rep <= 2)
+constexpr int PATTN_SMEM = (PATTN_QVEC * 128 + 32 * 129 + 32 * 128) * 4;
 
 __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ Q,
                                                            const int* __restrict__ row_off,
@@ -233,35 +237,35 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
                                                            int H, int n_rep, KVLayout kv, int layer,
                                                            float scale, float* __restrict__ out) {
     extern __shared__ float psm[];
-    float* Qs = psm;                  // [64][128]
-    float* Ks = psm + 64 * 128;       // [32][129]
+    float* Qs = psm;                     // [PATTN_QVEC][128]
+    float* Ks = psm + PATTN_QVEC * 128;  // [32][129]
     float* Vs = Ks + 32 * 129;        // [32][128]
     pdl_wait();
     pdl_trigger();
     const int qb = blockIdx.x, g = blockIdx.y, ri = blockIdx.z;
     const int L = row_len[ri], off = row_off[ri], row = row_id[ri];
-    const int q0 = qb * 32;
+    const int q0 = qb * PATTN_QP;
     if (q0 >= L) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int QV = 8;
+    constexpr int QV = PATTN_QVEC / 8;
     // query vector v: position q0 + v / n_rep, head g * n_rep + v % n_rep
-    for (int i = threadIdx.x; i < 64 * 128; i += 256) {
+    for (int i = threadIdx.x; i < PATTN_QVEC * 128; i += 256) {
         const int v = i >> 7, d = i & 127;
         const int p = q0 + v / n_rep, h = g * n_rep + v % n_rep;
-        Qs[i] = (p < L && v < 32 * n_rep) ? Q[(size_t)(off + p) * H * 128 + h * 128 + d] * scale : 0.f;
+        Qs[i] = (p < L && v < PATTN_QP * n_rep) ? Q[(size_t)(off + p) * H * 128 + h * 128 + d] * scale : 0.f;
     }
     float m[QV], l[QV], o[QV][4];
     int qpos[QV];
 #pragma unroll
     for (int j = 0; j < QV; ++j) {
         const int v = warp * QV + j;
-        qpos[j] = (v < 32 * n_rep) ? q0 + v / n_rep : 0x7fffffff;
+        qpos[j] = (v < PATTN_QP * n_rep) ? q0 + v / n_rep : 0x7fffffff;
         m[j] = -INFINITY;
         l[j] = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
     }
-    const int last_q = min(L - 1, q0 + 31);
+    const int last_q = min(L - 1, q0 + PATTN_QP - 1);
     for (int k0 = 0; k0 <= last_q; k0 += 32) {
         __syncthreads();
         for (int i = threadIdx.x; i < 32 * 128; i += 256) {
@@ -357,8 +361,9 @@ cudaError_t prefill_attn_launch(const float* Q, const int* row_off, const int* r
                                 const int* row_id, int n_rows, int max_L, int H, int n_rep,
                                 const KVLayout& kv, int layer, float scale, float* out,
                                 cudaStream_t s) {
-    if (n_rep < 1 || 32 * n_rep > 64) return cudaErrorInvalidValue;
-    return launch(prefill_attn_kernel, dim3((max_L + 31) / 32, kv.KVH, n_rows), dim3(256), PATTN_SMEM, s,
+    if (n_rep < 1 || PATTN_QP * n_rep > PATTN_QVEC) return cudaErrorInvalidValue;
+    return launch(prefill_attn_kernel, dim3((max_L + PATTN_QP - 1) / PATTN_QP, kv.KVH, n_rows), dim3(256),
+                  PATTN_SMEM, s,
                   false, Q, row_off, row_len, row_id, H, n_rep, kv, layer, scale, out);
 }
 
