@@ -220,13 +220,13 @@ __global__ void __launch_bounds__(256) prefill_qk_kernel(const float* __restrict
     }
 }
 
-// Causal attention of a row's prompt: grid (ceil(L/16), KVH, n_rows); each
-// CTA serves 16 query positions x n_rep heads (<= 32 query vectors, 4 per
+// Causal attention of a row's prompt: grid (ceil(L/8), KVH, n_rows); each
+// CTA serves 8 query positions x n_rep heads (<= 16 query vectors, 2 per
 // warp, staged pre-scaled in shared memory); keys and values stream through
 // shared memory 32 positions at a time with an online softmax.  The CTA of
 // the last query block walks every key block, so the query block is kept
 // small: that CTA's serial chain sets the kernel's time.
-constexpr int PATTN_QP = 16;                // query positions per CTA
+constexpr int PATTN_QP = 8;                 // query positions per CTA
 constexpr int PATTN_QVEC = 2 * PATTN_QP;    // query vectors per CTA (n_rep <= 2)
 constexpr int PATTN_SMEM = (PATTN_QVEC * 128 + 32 * 129 + 32 * 128) * 4;
 
