@@ -514,8 +514,10 @@ def config4_main(args, wl):
     model = SorakuModel.random(dims, 42, f"cuda:{local}")
     max_prompt = max(r[0].shape[1] + r[2].shape[0] + 2 for r in reqs)
     max_len = ((max_prompt + frames + 2 + 63) // 64) * 64
+    pbatch = min(n, 16)  # prompts per prefill pass
     eng = NativeEngine(model, max_requests=n, rows_per_request=2, max_len=max_len, max_frames=frames,
-                       max_prefill=max_prompt + 2, use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch)
+                       max_prefill=max_prompt + 2, use_pdl=not args.no_pdl, l2_prefetch=not args.no_prefetch,
+                       prefill_batch=pbatch)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -536,7 +538,10 @@ def config4_main(args, wl):
             eng.set_sampling(j, cfg=SAMPLING["cfg_scale"], temperature=0.9, temperature_q0=0.9, top_k=50,
                              top_p=0.95, top_k_q0=50, top_p_q0=0.95, seed=seed + 1000 * step,
                              min_new_frames=frames, eos_rule=1)
-            eng.prefill(j, ids, uncond, prompt)
+        for j0 in range(0, n, pbatch):  # several prompts per pass over the trunk
+            js = list(range(j0, min(n, j0 + pbatch)))
+            eng.prefill_many(js, [reqs[mine[j]][0] for j in js], [reqs[mine[j]][1] for j in js],
+                             [reqs[mine[j]][2] for j in js])
 
     prefill_all(0)
     eng.capture(n, fpg)

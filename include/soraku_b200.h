@@ -219,6 +219,8 @@ typedef struct {
                              tensor-core GEMM path (0 = 5); 1 makes every
                              batch take it, so a row's arithmetic does not
                              depend on the batch width                      */
+    int prefill_batch;    /* requests one skb_engine_prefill_many pass can
+                             hold (0 = 1); sizes the prefill scratch        */
     int kv_pages;         /* 0: every row owns ceil(max_len / page_size)
                              pages; > 0: a shared pool of this many pages
                              per layer, mapped to rows by
@@ -238,6 +240,14 @@ int skb_engine_destroy(skb_engine *eng);
 int skb_engine_prefill(skb_engine *eng, int request, const int64_t *cond_ids, int n_cond,
                        const int64_t *uncond_ids, int n_uncond, const int64_t *prompt_codes,
                        int n_prompt, const float *speaker, cudaStream_t stream);
+
+/* The prompts of n <= opts.prefill_batch distinct requests in one pass over
+ * the trunk (their tokens concatenated, so every GEMM sees all of them);
+ * arrays of n host pointers / counts as for skb_engine_prefill, without
+ * speaker vectors (route-D requests go through skb_engine_prefill). */
+int skb_engine_prefill_many(skb_engine *eng, int n, const int *requests, const int64_t *const *cond_ids,
+                            const int *n_cond, const int64_t *const *uncond_ids, const int *n_uncond,
+                            const int64_t *const *prompt_codes, const int *n_prompt, cudaStream_t stream);
 
 /* graph_frame.py:307-328 set_temperature/set_sampling/set_seed, per request.
  * top_k <= 0 or top_p outside (0,1) disable the filter; *_q0 apply to q0.

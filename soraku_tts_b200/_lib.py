@@ -48,6 +48,8 @@ SIGNATURES = {
     "skb_engine_status": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "skb_engine_move_request": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "skb_engine_map_pages": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p]),
+    "skb_engine_prefill_many": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_void_p]),
     "skb_engine_prefill": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
                                    c_void_p, c_void_p]),
     "skb_engine_set_sampling": (c_int, [c_void_p, c_int, c_float, c_float, c_float, c_int, c_float, c_int,
@@ -90,7 +92,7 @@ class skb_engine_opts(ctypes.Structure):
     _fields_ = [("max_requests", c_int), ("rows_per_request", c_int), ("max_len", c_int),
                 ("max_frames", c_int), ("max_prefill", c_int), ("page_size", c_int),
                 ("attn_splits", c_int), ("use_pdl", c_int), ("l2_prefetch", c_int), ("gemm_min_rows", c_int),
-                ("kv_pages", c_int)]
+                ("prefill_batch", c_int), ("kv_pages", c_int)]
 
 
 _lib = None

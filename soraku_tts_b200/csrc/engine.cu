@@ -79,7 +79,8 @@ struct skb_engine {
           *spk = nullptr, *spk_in = nullptr;
     PrefillTok* ptok = nullptr;
     int64_t* pframes = nullptr;
-    int* pmeta = nullptr;  // row_off | row_len | row_id | gather_src | gather_dst
+    int* pmeta = nullptr;  // [5][prefill rows]: row_off | row_len | row_id | gather_src | gather_dst
+    int prefill_batch = 1;  // requests one prefill pass can hold
     // graph
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -591,7 +592,9 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     e->layer_floats = (long long)n_pages * 2 * e->KVH * e->o.page_size * e->hd;
     const int qkvd = (e->H + 2 * e->KVH) * e->hd;
     const int actd = e->F > e->I ? e->F : e->I;
-    const int T = e->rpr * opts->max_prefill;
+    e->prefill_batch = opts->prefill_batch > 0 ? opts->prefill_batch : 1;
+    if (e->prefill_batch > e->nreq) e->prefill_batch = e->nreq;
+    const int T = e->prefill_batch * e->rpr * opts->max_prefill;
     int st = SKB_OK;
 #define A(ptr, n)                          \
     if (st == SKB_OK) st = dalloc(e, &ptr, (size_t)(n));
@@ -627,8 +630,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->spk, e->D)
     A(e->spk_in, m.speaker_dim > 0 ? m.speaker_dim : 1)
     A(e->ptok, T)
-    A(e->pframes, (size_t)(opts->max_prefill + 1) * e->Q)
-    A(e->pmeta, 5 * 8)
+    A(e->pframes, (size_t)e->prefill_batch * (opts->max_prefill + 1) * e->Q)
+    A(e->pmeta, (size_t)5 * e->prefill_batch * e->rpr)
 #undef A
     if (st != SKB_OK) {
         skb_engine_destroy(e);
@@ -730,64 +733,84 @@ int skb_engine_set_sampling(skb_engine* e, int req, float cfg, float temp, float
     return SKB_OK;
 }
 
-int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, const int64_t* uncond,
-                       int n_uncond, const int64_t* prompt, int n_prompt, const float* speaker,
-                       cudaStream_t s) {
-    if (!e || req < 0 || req >= e->nreq) return fail(SKB_ERR_ARG, "prefill: bad request");
-    if (!cond || n_cond < 1) return fail(SKB_ERR_ARG, "prefill: empty cond ids");
-    if (e->rpr == 2 && (!uncond || n_uncond < 1)) return fail(SKB_ERR_ARG, "prefill: CFG needs uncond ids");
-    if (n_prompt < 0 || (n_prompt > 0 && !prompt)) return fail(SKB_ERR_ARG, "prefill: bad prompt codes");
+// The prompts of n requests (reqs[i]'s cond / uncond ids, reference frames
+// and, for n == 1 only, speaker vector) through the trunk in one pass: their
+// tokens are concatenated (rows keep their own positions), so every GEMM of
+// the pass sees all of them.
+static int prefill_impl(skb_engine* e, int n, const int* reqs, const int64_t* const* conds, const int* n_conds,
+                        const int64_t* const* unconds, const int* n_unconds, const int64_t* const* prompts,
+                        const int* n_prompts, const float* speaker, cudaStream_t s) {
+    if (n < 1 || n > e->prefill_batch)
+        return fail(SKB_ERR_ARG, "prefill: %d requests (1..%d per pass, opts.prefill_batch)", n, e->prefill_batch);
     const skb_model_desc& m = e->m;
     const bool use_spk = speaker != nullptr;
     if (use_spk && !m.speaker_proj) return fail(SKB_ERR_ARG, "speaker embedding supplied to an unconditioned model");
     if (!use_spk && m.speaker_proj) return fail(SKB_ERR_ARG, "this model requires a speaker embedding");
+    if (use_spk && n != 1) return fail(SKB_ERR_ARG, "prefill: speaker vectors go one request per pass");
     const bool slot = use_spk && m.speaker_slot_mode;
     if (slot && !m.speaker_slot) return fail(SKB_ERR_ARG, "slot mode without speaker_slot_embedding");
-    // ids / codes validation
     auto is_lang = [&](int64_t id) {
         for (int j = 0; j < m.n_lang; ++j)
             if (m.lang_ids[j] == id) return true;
         return false;
     };
-    for (int b = 0; b < e->rpr; ++b) {
-        const int64_t* ids = b == 0 ? cond : uncond;
-        const int n = b == 0 ? n_cond : n_uncond;
-        for (int i = 0; i < n; ++i)
-            if ((ids[i] < 0 || ids[i] >= m.text_vocab) && !is_lang(ids[i]))
-                return fail(SKB_ERR_ARG, "prefill: text id %lld out of range", (long long)ids[i]);
+    for (int i = 0; i < n; ++i) {
+        const int req = reqs[i];
+        if (req < 0 || req >= e->nreq) return fail(SKB_ERR_ARG, "prefill: bad request %d", req);
+        for (int j = 0; j < i; ++j)
+            if (reqs[j] == req) return fail(SKB_ERR_ARG, "prefill: request %d given twice", req);
+        if (!conds[i] || n_conds[i] < 1) return fail(SKB_ERR_ARG, "prefill: empty cond ids");
+        if (e->rpr == 2 && (!unconds[i] || n_unconds[i] < 1)) return fail(SKB_ERR_ARG, "prefill: CFG needs uncond ids");
+        if (n_prompts[i] < 0 || (n_prompts[i] > 0 && !prompts[i])) return fail(SKB_ERR_ARG, "prefill: bad prompt codes");
+        for (int b = 0; b < e->rpr; ++b) {
+            const int64_t* ids = b == 0 ? conds[i] : unconds[i];
+            const int nn = b == 0 ? n_conds[i] : n_unconds[i];
+            for (int k = 0; k < nn; ++k)
+                if ((ids[k] < 0 || ids[k] >= m.text_vocab) && !is_lang(ids[k]))
+                    return fail(SKB_ERR_ARG, "prefill: text id %lld out of range", (long long)ids[k]);
+        }
+        for (int k = 0; k < n_prompts[i] * e->Q; ++k)
+            if (prompts[i][k] < 0 || prompts[i][k] >= e->V) return fail(SKB_ERR_ARG, "prefill: prompt code out of range");
     }
-    for (int i = 0; i < n_prompt * e->Q; ++i)
-        if (prompt[i] < 0 || prompt[i] >= e->V) return fail(SKB_ERR_ARG, "prefill: prompt code out of range");
+    // tokens of every row; each request's frames (audio BOS + prompt) in one array
+    const int NR = n * e->rpr;
     std::vector<PrefillTok> toks;
-    int row_off[2] = {0, 0}, row_len[2] = {0, 0}, row_id[2] = {0, 0};
-    for (int b = 0; b < e->rpr; ++b) {
-        const int row = req * e->rpr + b;
-        const int64_t* ids = b == 0 ? cond : uncond;
-        const int n = b == 0 ? n_cond : n_uncond;
-        row_off[b] = (int)toks.size();
-        int p = 0;
-        for (int i = 0; i < n; ++i) toks.push_back({row, p++, 0, (int)ids[i]});
-        if (slot) toks.push_back({row, p++, 2, 0});
-        for (int f = 0; f <= n_prompt; ++f) toks.push_back({row, p++, 1, f});
-        row_len[b] = p;
-        row_id[b] = row;
-        if (p > e->o.max_prefill || p >= e->o.max_len)
-            return fail(SKB_ERR_CAPACITY, "prefill %d exceeds max_prefill=%d / max_len=%d", p, e->o.max_prefill,
-                        e->o.max_len);
-        const int pst = check_pages(e, row, p);
-        if (pst) return pst;
+    std::vector<int> row_off(NR), row_len(NR), row_id(NR);
+    std::vector<int64_t> frames;
+    for (int i = 0; i < n; ++i) {
+        const int fbase = (int)(frames.size() / e->Q);
+        for (int q = 0; q < e->Q; ++q) frames.push_back(m.bos_id);
+        frames.insert(frames.end(), prompts[i], prompts[i] + (size_t)n_prompts[i] * e->Q);
+        for (int b = 0; b < e->rpr; ++b) {
+            const int k = i * e->rpr + b;
+            const int row = reqs[i] * e->rpr + b;
+            const int64_t* ids = b == 0 ? conds[i] : unconds[i];
+            const int nn = b == 0 ? n_conds[i] : n_unconds[i];
+            row_off[k] = (int)toks.size();
+            int p = 0;
+            for (int t = 0; t < nn; ++t) toks.push_back({row, p++, 0, (int)ids[t]});
+            if (slot) toks.push_back({row, p++, 2, 0});
+            for (int f = 0; f <= n_prompts[i]; ++f) toks.push_back({row, p++, 1, fbase + f});
+            row_len[k] = p;
+            row_id[k] = row;
+            if (p > e->o.max_prefill || p >= e->o.max_len)
+                return fail(SKB_ERR_CAPACITY, "prefill %d exceeds max_prefill=%d / max_len=%d", p, e->o.max_prefill,
+                            e->o.max_len);
+            const int pst = check_pages(e, row, p);
+            if (pst) return pst;
+        }
     }
     const int T = (int)toks.size();
-    std::vector<int64_t> frames((size_t)(n_prompt + 1) * e->Q);
-    for (int q = 0; q < e->Q; ++q) frames[q] = m.bos_id;
-    for (int i = 0; i < n_prompt * e->Q; ++i) frames[e->Q + i] = prompt[i];
-    int meta[5 * 8] = {0};
-    for (int b = 0; b < e->rpr; ++b) {
-        meta[0 + b] = row_off[b];
-        meta[8 + b] = row_len[b];
-        meta[16 + b] = row_id[b];
-        meta[24 + b] = row_off[b] + row_len[b] - 1;
-        meta[32 + b] = row_id[b];
+    const int RC = e->prefill_batch * e->rpr;  // pmeta stride
+    std::vector<int> meta((size_t)5 * RC, 0);
+    int maxL = 0;
+    for (int k = 0; k < NR; ++k) {
+        meta[0 * RC + k] = row_off[k];
+        meta[1 * RC + k] = row_len[k];
+        meta[2 * RC + k] = row_id[k];
+        meta[3 * RC + k] = row_off[k] + row_len[k] - 1;
+        meta[4 * RC + k] = row_id[k];
+        maxL = row_len[k] > maxL ? row_len[k] : maxL;
     }
     cudaError_t err = cudaSuccess;
 #define CK(x)                                                                        \
@@ -797,19 +820,18 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
     } while (0)
     CK(cudaMemcpyAsync(e->ptok, toks.data(), sizeof(PrefillTok) * T, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(e->pframes, frames.data(), frames.size() * 8, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(e->pmeta, meta, sizeof meta, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(e->pmeta, meta.data(), sizeof(int) * meta.size(), cudaMemcpyHostToDevice, s));
     const float* bos_add = nullptr;
     if (use_spk) {
         CK(cudaMemcpyAsync(e->spk_in, speaker, sizeof(float) * m.speaker_dim, cudaMemcpyHostToDevice, s));
         CK(speaker_launch(e->spk_in, m.speaker_dim, m.speaker_proj, e->D, slot ? m.speaker_slot : nullptr, e->spk, s));
-        if (!slot) bos_add = e->spk;
+        if (!slot) bos_add = e->spk;  // (one request: its audio BOS frame is frame 0)
     }
     CK(prefill_embed_launch(e->ptok, T, m.embed_tokens, m.text_vocab, m.lang_embed, m.n_lang, m.lang_ids,
                             e->pframes, e->Q, m.table, e->V, m.frame_scale, e->spk, bos_add, e->pX, e->D,
                             e->err + 1, s));
     const KVLayout kv = kv_layout(e);
     const int qd = e->H * e->hd, kvd = e->KVH * e->hd;
-    const int maxL = row_len[0] > row_len[1] ? row_len[0] : row_len[1];
     for (int l = 0; l < e->L; ++l) {
         int stt = rmsnorm_rows(e->pX, nullptr, LW(e, l, W_LN1), e->pN, T, e->D, m.rms_eps, s, false);
         if (stt) return stt;
@@ -830,7 +852,7 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         CK(tgemm_launch(g, s));
         CK(prefill_qk_launch(e->pQKV, qd + 2 * kvd, e->ptok, T, LW(e, l, W_QN), LW(e, l, W_KN), m.rms_eps,
                              e->rope_cos, e->rope_sin, e->H, kv, l, e->pQ, s));
-        CK(prefill_attn_launch(e->pQ, e->pmeta, e->pmeta + 8, e->pmeta + 16, e->rpr, maxL, e->H, e->n_rep, kv, l,
+        CK(prefill_attn_launch(e->pQ, e->pmeta, e->pmeta + RC, e->pmeta + 2 * RC, NR, maxL, e->H, e->n_rep, kv, l,
                                1.0f / sqrtf((float)e->hd), e->pA, s));
         GemmArgs o = {};
         o.A = e->pA;
@@ -876,19 +898,46 @@ int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, 
         dn.mode = 1;
         CK(tgemm_launch(dn, s));
     }
-    CK(gather_rows_launch(e->pX, e->pmeta + 24, e->pmeta + 32, e->rpr, e->x, e->D, s));
-    // positions, prefix, counters
-    int posv[2] = {row_len[0], row_len[1]};
-    CK(cudaMemcpyAsync(e->pos + req * e->rpr, posv, sizeof(int) * e->rpr, cudaMemcpyHostToDevice, s));
-    CK(cudaMemsetAsync(e->prefix + (size_t)req * e->D, 0, sizeof(float) * e->D, s));
-    int zero2[2] = {0, 0};
-    CK(cudaMemcpyAsync(reinterpret_cast<char*>(e->st + req) + offsetof(ReqState, frame), zero2, sizeof zero2,
-                       cudaMemcpyHostToDevice, s));
+    CK(gather_rows_launch(e->pX, e->pmeta + 3 * RC, e->pmeta + 4 * RC, NR, e->x, e->D, s));
+    // positions, prefix, counters of each request
+    for (int i = 0; i < n; ++i) {
+        const int req = reqs[i];
+        CK(cudaMemcpyAsync(e->pos + req * e->rpr, row_len.data() + i * e->rpr, sizeof(int) * e->rpr,
+                           cudaMemcpyHostToDevice, s));
+        CK(cudaMemsetAsync(e->prefix + (size_t)req * e->D, 0, sizeof(float) * e->D, s));
+        static const int zero2[2] = {0, 0};
+        CK(cudaMemcpyAsync(reinterpret_cast<char*>(e->st + req) + offsetof(ReqState, frame), zero2, sizeof zero2,
+                           cudaMemcpyHostToDevice, s));
+    }
     CK(cudaStreamSynchronize(s));
 #undef CK
-    for (int b = 0; b < e->rpr; ++b) e->pos_host[req * e->rpr + b] = row_len[b];
-    e->frames_host[req] = 0;
+    for (int i = 0; i < n; ++i) {
+        for (int b = 0; b < e->rpr; ++b) e->pos_host[reqs[i] * e->rpr + b] = row_len[i * e->rpr + b];
+        e->frames_host[reqs[i]] = 0;
+    }
     return SKB_OK;
+}
+
+int skb_engine_prefill(skb_engine* e, int req, const int64_t* cond, int n_cond, const int64_t* uncond,
+                       int n_uncond, const int64_t* prompt, int n_prompt, const float* speaker,
+                       cudaStream_t s) {
+    if (!e) return fail(SKB_ERR_ARG, "prefill: null engine");
+    return prefill_impl(e, 1, &req, &cond, &n_cond, &uncond, &n_uncond, &prompt, &n_prompt, speaker, s);
+}
+
+int skb_engine_prefill_many(skb_engine* e, int n, const int* requests, const int64_t* const* cond_ids,
+                            const int* n_cond, const int64_t* const* uncond_ids, const int* n_uncond,
+                            const int64_t* const* prompt_codes, const int* n_prompt, cudaStream_t s) {
+    if (!e || n < 1 || !requests || !cond_ids || !n_cond || !n_prompt || (e->rpr == 2 && (!uncond_ids || !n_uncond)))
+        return fail(SKB_ERR_ARG, "prefill_many: bad arguments");
+    std::vector<const int64_t*> unc(n, nullptr), pc(n, nullptr);
+    std::vector<int> nu(n, 0);
+    for (int i = 0; i < n; ++i) {
+        if (uncond_ids) unc[i] = uncond_ids[i];
+        if (n_uncond) nu[i] = n_uncond[i];
+        if (prompt_codes) pc[i] = prompt_codes[i];
+    }
+    return prefill_impl(e, n, requests, cond_ids, n_cond, unc.data(), nu.data(), pc.data(), n_prompt, nullptr, s);
 }
 
 int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream) {

@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -41,12 +42,13 @@ class NativeEngine:
 
     def __init__(self, model, *, max_requests=1, rows_per_request=2, max_len=1024, max_frames=1024,
                  max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True, gemm_min_rows=0,
-                 kv_pages=0):
+                 prefill_batch=1, kv_pages=0):
         self.model = model
         opts = _lib.skb_engine_opts(max_requests, rows_per_request, max_len, max_frames,
                                     max_prefill if max_prefill else max_len, page_size, attn_splits,
                                     1 if use_pdl else 0, 1 if l2_prefetch else 0, int(gemm_min_rows),
-                                    int(kv_pages))
+                                    int(prefill_batch), int(kv_pages))
+        self.prefill_batch = max(1, int(prefill_batch))
         self.page_size = page_size
         handle = ctypes.c_void_p()
         desc = model.model_desc()
@@ -84,6 +86,28 @@ class NativeEngine:
                   unc.data_ptr() if unc is not None else None, unc.numel() if unc is not None else 0,
                   pc.data_ptr() if pc is not None else None, n_prompt,
                   spk.data_ptr() if spk is not None else None, _lib.stream_ptr(stream))
+
+    def prefill_many(self, requests, cond_ids, uncond_ids, prompt_codes, stream=None):
+        """Prompts of several requests in one pass (no speaker vectors):
+        sequences of per-request cond ids, uncond ids and prompt codes."""
+        n = len(requests)
+        conds = [_host_ids(c) for c in cond_ids]
+        uncs = [_host_ids(u) for u in uncond_ids]
+        pcs = []
+        for pc in prompt_codes:
+            t = torch.as_tensor(pc if pc is not None else np.zeros((0, self.Q), np.int64))
+            pcs.append(t.to("cpu", torch.int64).reshape(-1, self.Q).contiguous())
+        P = ctypes.c_void_p
+        req_a = (ctypes.c_int * n)(*[int(r) for r in requests])
+        c_ptr = (P * n)(*[c.data_ptr() for c in conds])
+        c_n = (ctypes.c_int * n)(*[c.numel() for c in conds])
+        u_ptr = (P * n)(*[u.data_ptr() for u in uncs])
+        u_n = (ctypes.c_int * n)(*[u.numel() for u in uncs])
+        p_ptr = (P * n)(*[(p.data_ptr() if p.numel() else None) for p in pcs])
+        p_n = (ctypes.c_int * n)(*[p.shape[0] for p in pcs])
+        _lib.call("skb_engine_prefill_many", self.h, n, ctypes.addressof(req_a), ctypes.addressof(c_ptr),
+                  ctypes.addressof(c_n), ctypes.addressof(u_ptr), ctypes.addressof(u_n), ctypes.addressof(p_ptr),
+                  ctypes.addressof(p_n), _lib.stream_ptr(stream))
 
     def set_sampling(self, request, *, cfg, temperature, temperature_q0, top_k, top_p, top_k_q0, top_p_q0,
                      seed, min_new_frames=0, eos_rule=0):

@@ -19,8 +19,12 @@ finishes, so short requests do not reserve a full ``max_len`` per row.
 Determinism: every request draws from its own Philox stream (counter =
 (stream 0, frame, q) under the request's seed), the engine runs the
 tensor-core GEMM path for every batch width and fixes the attention kernel
-variant, so a request's codes do not depend on its slot, on the requests
-beside it or on when it was admitted.
+variant, so a request's decode does not depend on its slot or on the
+requests beside it.  Requests admitted together share one prompt pass
+(``prefill_many``); while that pass holds at most 128 tokens its arithmetic
+per token is the same as a pass of one prompt, beyond that the GEMM's K
+split follows the token count and the prompt's hidden state can differ in
+the last FP32 bits (``prefill_per_pass=1`` keeps one prompt per pass).
 
 Semantics per request are ``FastGenerator.generate``'s: CFG ``u + s (c - u)``,
 EOS only at q0 from frame ``min_new_frames`` on, which ends the utterance
@@ -97,7 +101,7 @@ class ContinuousBatcher:
 
     def __init__(self, model, *, slots: int, max_len: int, max_frames: int, frames_per_graph: int = 4,
                  max_prefill: int | None = None, kv_pages: int | None = None, page_size: int = 64,
-                 device: Any = "cuda", engine_factory=None, **engine_kw):
+                 prefill_per_pass: int = 8, device: Any = "cuda", engine_factory=None, **engine_kw):
         self.model = as_soraku_model(model, torch.device(device)) if engine_factory is None else model
         cfg = self.model.config
         self.Q = int(cfg.num_codebooks)
@@ -111,7 +115,7 @@ class ContinuousBatcher:
         make = engine_factory or (lambda **kw: NativeEngine(self.model, **kw))
         # every batch width on the tensor-core path; one attention split per
         # (row, kv head): a row's arithmetic is the same at every width
-        kw = dict(gemm_min_rows=1, attn_splits=1)
+        kw = dict(gemm_min_rows=1, attn_splits=1, prefill_batch=max(1, min(slots, prefill_per_pass)))
         kw.update(engine_kw)
         self.page_size = int(page_size)
         self.max_pages = -(-self.max_len // self.page_size)
@@ -224,35 +228,51 @@ class ContinuousBatcher:
             self.stats["moves"] += 1
 
     def _admit(self) -> None:
+        """Fill free slots from the queue (in arrival order), then prefill the
+        admitted prompts, several per pass over the trunk."""
+        batch = []
         for j in range(len(self.slots)):
-            if not self.queue:
-                return
             if self.slots[j] is not None:
                 continue
-            req = self.queue.popleft()
-            if req.max_new_frames == 0:  # nothing to decode
-                self.results[req.rid] = np.zeros((0, self.Q), np.int64)
-                self.stop_reason[req.rid] = "max_frames"
-                continue
-            e = self.engine
-            pages = []
-            if self.pool is not None:
-                need = self._pages_needed(req)
-                if sum(need) > self.pool.available():  # wait for pages, keeping arrival order
-                    self.queue.appendleft(req)
-                    return
-                for b, k in enumerate(need):
-                    got = self.pool.take(k)
-                    e.map_pages(2 * j + b, 0, got + [-1] * (self.max_pages - k))
-                    pages.append(got)
-            e.set_sampling(j, cfg=req.cfg_scale, temperature=req.temperature,
-                           temperature_q0=req.temperature if req.temperature_q0 is None else req.temperature_q0,
-                           top_k=req.top_k, top_p=req.top_p, top_k_q0=req.top_k, top_p_q0=req.top_p,
-                           seed=req.seed, min_new_frames=req.min_new_frames, eos_rule=1)
-            e.set_rng_stream(j, 0)
-            e.prefill(j, req.input_ids, self._uncond(req), req.prompt_codes, req.speaker)
-            self.slots[j] = _Slot(req, pages=pages)
-            self.stats["admitted"] += 1
+            while self.queue:
+                req = self.queue.popleft()
+                if req.max_new_frames == 0:  # nothing to decode
+                    self.results[req.rid] = np.zeros((0, self.Q), np.int64)
+                    self.stop_reason[req.rid] = "max_frames"
+                    continue
+                pages = []
+                if self.pool is not None:
+                    need = self._pages_needed(req)
+                    if sum(need) > self.pool.available():  # wait for pages, keeping arrival order
+                        self.queue.appendleft(req)
+                        break
+                    for b, k in enumerate(need):
+                        got = self.pool.take(k)
+                        self.engine.map_pages(2 * j + b, 0, got + [-1] * (self.max_pages - k))
+                        pages.append(got)
+                self.engine.set_sampling(
+                    j, cfg=req.cfg_scale, temperature=req.temperature,
+                    temperature_q0=req.temperature if req.temperature_q0 is None else req.temperature_q0,
+                    top_k=req.top_k, top_p=req.top_p, top_k_q0=req.top_k, top_p_q0=req.top_p, seed=req.seed,
+                    min_new_frames=req.min_new_frames, eos_rule=1)
+                self.engine.set_rng_stream(j, 0)
+                self.slots[j] = _Slot(req, pages=pages)
+                self.stats["admitted"] += 1
+                batch.append((j, req))
+                break
+            else:
+                break  # queue empty
+            if self.slots[j] is None:
+                break  # the head request waits for pages
+        per_pass = max(1, int(getattr(self.engine, "prefill_batch", 1)))
+        plain = [(j, r) for j, r in batch if r.speaker is None]
+        for i in range(0, len(plain), per_pass):
+            chunk = plain[i:i + per_pass]
+            self.engine.prefill_many([j for j, _ in chunk], [r.input_ids for _, r in chunk],
+                                     [self._uncond(r) for _, r in chunk], [r.prompt_codes for _, r in chunk])
+        for j, r in batch:
+            if r.speaker is not None:
+                self.engine.prefill(j, r.input_ids, self._uncond(r), r.prompt_codes, r.speaker)
 
     def _collect(self, j: int, frames: int) -> None:
         s = self.slots[j]

@@ -39,6 +39,7 @@ class FakeEngine:
         self.st = [dict(seed=0, min=0, frame=0, done=0, stream=i, pos=0) for i in range(max_requests)]
         self.hist = np.zeros((max_requests, max_frames, Q), np.int64)
         self.graph = None
+        self.prefill_batch = kw.get("prefill_batch", 1)
         self.kw = kw
         self.log = []
 
@@ -69,6 +70,11 @@ class FakeEngine:
         self._check_pages(2 * j + 1, lu)
         self.st[j].update(frame=0, done=0, pos=lc, upos=lu)
         self.log.append(("prefill", j))
+
+    def prefill_many(self, js, conds, uncs, prompts):
+        assert len(js) <= self.prefill_batch
+        for j, c, u, p in zip(js, conds, uncs, prompts):
+            self.prefill(j, c, u, p, None)
 
     def capture(self, n, fpg):
         self.graph = (n, fpg)
