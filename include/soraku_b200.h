@@ -259,7 +259,9 @@ int skb_engine_set_sampling(skb_engine *eng, int request, float cfg_scale, float
 
 /* graph_frame.py:274-296 capture: records frames_per_graph whole frames
  * (16 depth steps with sampling, frame embedding, one trunk step) for the
- * first n_active requests as one CUDA graph. */
+ * first n_active requests as one CUDA graph.  The engine keeps the 16 most
+ * recently used (n_active, frames_per_graph) graphs, so returning to a batch
+ * width captured before costs no new capture. */
 int skb_engine_capture(skb_engine *eng, int n_active, int frames_per_graph, cudaStream_t stream);
 
 /* graph_frame.py:298-305 step_frame: replays the graph once (frames_per_graph

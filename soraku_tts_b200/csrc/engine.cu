@@ -85,6 +85,14 @@ struct skb_engine {
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t exec = nullptr;
     int graph_active = 0, graph_fpg = 0, graph_pdl = 0;
+    // captured graphs by (batch width, frames per replay), least recently used evicted
+    struct CachedGraph {
+        int n_active, fpg, pdl;
+        cudaGraphExec_t exec;
+        unsigned long long used;
+    };
+    std::vector<CachedGraph> graphs;
+    unsigned long long graph_clock = 0;
     int debug = 0;
     float* xn = nullptr;  // batched path: normalised activations [R][max inner size]
     int gemm_min_rows = 5;  // batches of at least this many rows take the tensor-core GEMM path
@@ -501,8 +509,12 @@ int run_frames(skb_engine* e, const std::vector<Node>& nodes, int frames, cudaSt
     return SKB_OK;
 }
 
+constexpr size_t GRAPH_CACHE = 16;
+
+// Drops every captured graph (the frame program changed, or the engine goes).
 void destroy_graph(skb_engine* e) {
-    if (e->exec) cudaGraphExecDestroy(e->exec);
+    for (auto& g : e->graphs) cudaGraphExecDestroy(g.exec);
+    e->graphs.clear();
     e->exec = nullptr;
     e->graph_active = 0;
     e->graph_fpg = 0;
@@ -944,7 +956,23 @@ int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream
     if (!e) return fail(SKB_ERR_ARG, "capture: null engine");
     if (n_active < 1 || n_active > e->nreq || fpg < 1 || fpg > 64)
         return fail(SKB_ERR_ARG, "capture: n_active %d (1..%d), frames_per_graph %d (1..64)", n_active, e->nreq, fpg);
-    destroy_graph(e);
+    for (auto& g : e->graphs)
+        if (g.n_active == n_active && g.fpg == fpg) {  // captured before: reuse it
+            g.used = ++e->graph_clock;
+            e->exec = g.exec;
+            e->graph_active = n_active;
+            e->graph_fpg = fpg;
+            e->graph_pdl = g.pdl;
+            return SKB_OK;
+        }
+    if (e->graphs.size() >= GRAPH_CACHE) {
+        size_t lru = 0;
+        for (size_t i = 1; i < e->graphs.size(); ++i)
+            if (e->graphs[i].used < e->graphs[lru].used) lru = i;
+        if (e->graphs[lru].exec == e->exec) e->exec = nullptr;
+        cudaGraphExecDestroy(e->graphs[lru].exec);
+        e->graphs.erase(e->graphs.begin() + (long)lru);
+    }
     cudaStream_t cs = e->cap_stream;
     cudaError_t err = cudaStreamSynchronize(stream);
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "capture sync: %s", cudaGetErrorString(err));
@@ -973,6 +1001,7 @@ int skb_engine_capture(skb_engine* e, int n_active, int fpg, cudaStream_t stream
         e->graph_active = n_active;
         e->graph_fpg = fpg;
         e->graph_pdl = pdl ? 1 : 0;
+        e->graphs.push_back({n_active, fpg, e->graph_pdl, e->exec, ++e->graph_clock});
         return SKB_OK;
     }
     return fail(SKB_ERR_CUDA, "capture failed");
