@@ -1,6 +1,8 @@
-// Trunk kernels: decode attention (split over the KV positions, last-CTA
-// combine) and the prefill path (embedding, SIMT FP32 GEMM, q/k norm + RoPE +
-// KV write, causal attention).
+// Trunk kernels: decode attention for more than 8 splits per (row, kv head)
+// (split over the KV positions, last-CTA combine), the prefill path
+// (embedding, q/k norm + RoPE + KV write, causal attention; its projections
+// run on the tensor-core GEMM of tgemm.cu), and the SIMT FP32 GEMM that
+// skb_test_gemm keeps as the comparison path of the tensor-core one.
 #include "ops.cuh"
 #include "trunk.cuh"
 #include "trunk_api.cuh"
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(256) speaker_kernel(const float* __restrict__ 
     }
 }
 
+// SIMT FP32 GEMM (skb_test_gemm tensor_cores = 0):
 // C[t][n] = sum_k A[t][k] W(n)[k], 64x64 tiles, BK 16, 4x4 per thread.
 __device__ __forceinline__ const float* gemm_row(const GemmArgs& a, int n) {
     if (a.interleave) return ((n & 1) ? a.w1 : a.w0) + (size_t)(n >> 1) * a.K;
