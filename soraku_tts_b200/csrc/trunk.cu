@@ -226,9 +226,10 @@ __global__ void __launch_bounds__(256) prefill_qk_kernel(const float* __restrict
 // Causal attention of a row's prompt: grid (ceil(L/8), KVH, n_rows); each
 // CTA serves 8 query positions x n_rep heads (<= 16 query vectors, 2 per
 // warp, staged pre-scaled in shared memory); keys and values stream through
-// shared memory 32 positions at a time with an online softmax.  The CTA of
-// the last query block walks every key block, so the query block is kept
-// small: that CTA's serial chain sets the kernel's time.
+// shared memory 32 positions at a time with an online softmax, the next
+// block's loads in flight during this block's math.  The CTA of the last
+// query block walks every key block, so the query block is kept small: that
+// CTA's serial chain sets the kernel's time.
 constexpr int PATTN_QP = 8;                 // query positions per CTA
 constexpr int PATTN_QVEC = 2 * PATTN_QP;    // query vectors per CTA (n_rep <= 2)
 constexpr int PATTN_SMEM = (PATTN_QVEC * 128 + 32 * 129 + 32 * 128) * 4;
@@ -269,20 +270,38 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
         for (int c = 0; c < 4; ++c) o[j][c] = 0.f;
     }
     const int last_q = min(L - 1, q0 + PATTN_QP - 1);
+    // K/V blocks of 32 positions: thread t loads position t / 8 of the block,
+    // float4 columns t % 8 + 8 j (one page lookup per thread), into registers
+    // one block ahead, so the next block's loads are in flight during this
+    // block's math.
+    const int lk = threadIdx.x >> 3, lc = threadIdx.x & 7;
+    float4 kr[4], vr[4];
+    auto load_block = [&](int k0) {
+        const int p = k0 + lk;
+        const bool ok = p < L;
+        const float4* kb = ok ? reinterpret_cast<const float4*>(kv.at(layer, row, p, 0, g)) : nullptr;
+        const float4* vb = ok ? reinterpret_cast<const float4*>(kv.at(layer, row, p, 1, g)) : nullptr;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            kr[j] = ok ? __ldcg(kb + lc + 8 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vr[j] = ok ? __ldcg(vb + lc + 8 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    load_block(0);
     for (int k0 = 0; k0 <= last_q; k0 += 32) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < 32 * 128; i += 256) {
-            const int kk = i >> 7, d = i & 127;
-            const int p = k0 + kk;
-            float kk_v = 0.f, vv = 0.f;
-            if (p < L) {
-                kk_v = kv.at(layer, row, p, 0, g)[d];
-                vv = kv.at(layer, row, p, 1, g)[d];
-            }
-            Ks[kk * 129 + d] = kk_v;
-            Vs[kk * 128 + d] = vv;
+        __syncthreads();  // the previous block's math is done with Ks / Vs
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int d = 4 * (lc + 8 * j);
+            float* kd = Ks + lk * 129 + d;
+            kd[0] = kr[j].x;
+            kd[1] = kr[j].y;
+            kd[2] = kr[j].z;
+            kd[3] = kr[j].w;
+            *reinterpret_cast<float4*>(Vs + lk * 128 + d) = vr[j];
         }
         __syncthreads();
+        if (k0 + 32 <= last_q) load_block(k0 + 32);
         const int p = k0 + lane;
         float sdot[QV];
 #pragma unroll
