@@ -231,6 +231,23 @@ def main():
     if want("model_full"):
         make_model_case("model_full", ModelDims(), seed=42, random_norms=False, random_bias=False,
                         n_text=48, n_ref=72, n_frames=2, record_q=[0, 15], greedy_frames=0)
+    if want("model_route_d_full"):
+        # config 3 at benchmark size: 28 layers, four language IDs, slot-mode
+        # speaker vector (seed 7), text and reference lengths drawn from
+        # U[16, 96] and U[24, 144]
+        rng = np.random.default_rng(3)
+        n_text, n_ref = int(rng.integers(16, 97)), int(rng.integers(24, 145))
+        s = SorakuV2Config(language_token_ids=(151669, 151670, 151671, 151672), speaker_conditioning=True,
+                           speaker_condition_mode="slot")
+        make_model_case("model_route_d_full", ModelDims(s), seed=42, random_norms=False, random_bias=False,
+                        n_text=n_text, n_ref=n_ref, n_frames=2, record_q=[0, 15], language=2, speaker_seed=7,
+                        ids_seed=77)
+    if want("model_bos"):
+        # speaker vector added to the audio-BOS frame (model.py:649-651)
+        s = SorakuV2Config(speaker_conditioning=True, speaker_condition_mode="bos")
+        make_model_case("model_bos", ModelDims(s, small_trunk), seed=9, random_norms=True,
+                        random_bias=True, n_text=14, n_ref=7, n_frames=2, record_q=[0, 5, 15],
+                        speaker_seed=8)
 
 
 if __name__ == "__main__":

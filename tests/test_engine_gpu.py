@@ -45,6 +45,20 @@ def route_d():
 
 
 @pytest.fixture(scope="module")
+def bos_mode():
+    data, meta = load_golden("model_bos")
+    orc, dims, sd = oracle_from_meta(meta)
+    return data, meta, orc, _gpu_model(dims, sd)
+
+
+@pytest.fixture(scope="module")
+def full_route_d():
+    data, meta = load_golden("model_route_d_full")
+    orc, dims, sd = oracle_from_meta(meta)
+    return data, meta, orc, _gpu_model(dims, sd)
+
+
+@pytest.fixture(scope="module")
 def full():
     data, meta = load_golden("model_full")
     orc, dims, sd = oracle_from_meta(meta)
@@ -280,3 +294,24 @@ def test_full_model_config1_prefill_and_decode(full):
     codes, logits, hidden0 = _decode(model, data, 16, seed=42)
     assert_close(hidden0, data["hidden"][0], what="full prefill hidden (vs reference golden)", **TOL)
     _check_frames(orc, data, meta, codes, logits, temperature=0.9, top_k=50, top_p=0.95, seed=42)
+
+
+def test_speaker_bos_mode(bos_mode):
+    """Speaker vector added to the audio-BOS frame (model.py:649-651): prefill
+    hidden against the reference golden, then decoded frames against the oracle."""
+    data, meta, orc, model = bos_mode
+    spk = data["speaker"][0]
+    codes, logits, hidden0 = _decode(model, data, 3, seed=56, speaker=spk)
+    assert_close(hidden0, data["hidden"][0], what="bos-mode prefill hidden (vs reference golden)", **TOL)
+    _check_frames(orc, data, meta, codes, logits, temperature=0.9, top_k=50, top_p=0.95, seed=56, speaker=spk)
+
+
+def test_full_model_route_d_config3(full_route_d):
+    """Config 3 at benchmark size: 28 layers, language ID, slot-mode speaker,
+    text/reference lengths drawn from U[16, 96] / U[24, 144]; prefill hidden
+    against the reference golden and 8 decoded frames against the oracle."""
+    data, meta, orc, model = full_route_d
+    spk = data["speaker"][0]
+    codes, logits, hidden0 = _decode(model, data, 8, seed=31, speaker=spk)
+    assert_close(hidden0, data["hidden"][0], what="route-D full prefill hidden (vs reference golden)", **TOL)
+    _check_frames(orc, data, meta, codes, logits, temperature=0.9, top_k=50, top_p=0.95, seed=31, speaker=spk)

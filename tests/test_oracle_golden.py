@@ -9,7 +9,7 @@ import pytest
 from oracle import sampler as osamp
 from tests._util import assert_close, load_golden, oracle_from_meta
 
-TOL = dict(rtol=1e-4, atol=1e-4)  # logits within rel/abs 1e-4
+TOL = dict(rtol=1e-4, atol=1e-4)  # logits and hidden states within rel/abs 1e-4
 
 
 def _teacher(name):
@@ -23,7 +23,7 @@ def _teacher(name):
     return data, meta, orc, out
 
 
-@pytest.mark.parametrize("name", ["model_small", "model_route_d"])
+@pytest.mark.parametrize("name", ["model_small", "model_route_d", "model_bos"])
 def test_oracle_teacher_forced_small(name):
     data, meta, _, out = _teacher(name)
     assert_close(out["hidden"], data["hidden"], what=f"{name} hidden", **TOL)
@@ -37,6 +37,16 @@ def test_oracle_teacher_forced_full_model():
     data, meta, _, out = _teacher("model_full")
     assert_close(out["hidden"], data["hidden"], what="full hidden", **TOL)
     assert_close(out["logits"], data["logits"], what="full logits", **TOL)
+
+
+@pytest.mark.slow
+def test_oracle_teacher_forced_full_route_d():
+    """28 layers, route D (config 3): language ID, slot-mode speaker vector,
+    text and reference lengths drawn from U[16, 96] and U[24, 144]."""
+    data, meta, _, out = _teacher("model_route_d_full")
+    assert_close(out["hidden"], data["hidden"], what="route-D full hidden", **TOL)
+    assert_close(out["logits"], data["logits"], what="route-D full logits", **TOL)
+    assert_close(out["hidden_after"], data["hidden_after"], what="route-D full hidden_after", **TOL)
 
 
 def test_oracle_greedy_generate_matches_reference():

@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import sampler as osamp
 from tests._util import load_golden, oracle_from_meta
 
 pytestmark = pytest.mark.gpu
@@ -25,7 +26,7 @@ def small():
 
     data, meta = load_golden("model_small")
     orc, dims, sd = oracle_from_meta(meta)
-    return data, SorakuModel(dims, sd, "cuda")
+    return data, SorakuModel(dims, sd, "cuda"), orc
 
 
 def _requests(data):
@@ -77,7 +78,7 @@ def test_continuous_batching_equals_static_batch(small, kv_pages):
     needs 3-4), so admission also waits for free pages."""
     from soraku_tts_b200.scheduler import ContinuousBatcher, DecodeRequest
 
-    data, model = small
+    data, model, _ = small
     reqs = _requests(data)
     want = _static(model, reqs)
     streamed = {}
@@ -96,3 +97,48 @@ def test_continuous_batching_equals_static_batch(small, kv_pages):
     if kv_pages:
         assert b.pool.available() == kv_pages
     b.close()
+
+
+def test_continuous_batching_matches_oracle(small):
+    """Every request of a continuous run (joins, leaves, slot moves) against the
+    oracle teacher-forced on that request's own codes: each emitted code is the
+    oracle sampler's draw from the oracle's logits with the request's Philox
+    uniform (stream 0, its own seed); a code may differ only where the oracle's
+    draw flips under a shift of the uniform by 1e-4 (logits agree within
+    rel/abs 1e-4, so a draw that close to a CDF boundary may go either way), and
+    no more than 1 % of draws may sit that close.  A request that stopped on EOS
+    must be one whose next q0 draw is EOS in the oracle."""
+    from soraku_tts_b200.scheduler import ContinuousBatcher, DecodeRequest
+
+    data, model, orc = small
+    reqs = _requests(data)
+    b = ContinuousBatcher(model, slots=3, max_len=512, max_frames=64, frames_per_graph=2)
+    for r in reqs:
+        b.submit(DecodeRequest(**r))
+    got = b.run()
+    assert b.stats["moves"] > 0
+    near = total = 0
+    for r in reqs:
+        codes = got[r["rid"]]
+        stopped_eos = b.stop_reason[r["rid"]] == "eos"
+        n = codes.shape[0]
+        check = np.concatenate([codes, np.zeros((1, 16), np.int64)]) if stopped_eos else codes
+        if check.shape[0] == 0:
+            continue
+        tf = orc.teacher_forced(input_ids=r["input_ids"][0], uncond_input_ids=r["uncond_ids"][0],
+                                prompt_codes=r["prompt_codes"], codes=check, cfg_scale=1.5)
+        for f in range(check.shape[0]):
+            for q in range(16 if f < n else 1):
+                c, u = tf["logits"][f, q, 0], tf["logits"][f, q, 1]
+                kw = dict(cfg=1.5, temperature=0.9, top_k=50, top_p=0.95,
+                          mask_eos=(q != 0 or f < r["min_new_frames"]), bos=2048, pad=2050, eos=EOS)
+                uni = osamp.uniform(r["seed"], 0, f, q)
+                want = osamp.sample(c, u, u=uni, **kw)
+                have = EOS if f == n else int(codes[f, q])
+                total += 1
+                if have != want:
+                    alt = {osamp.sample(c, u, u=min(max(uni + d, 0.0), 1.0 - 2 ** -24), **kw) for d in (-1e-4, 1e-4)}
+                    assert have in alt, f"request {r['rid']} frame {f} q {q}: {have} vs oracle {want}"
+                    near += 1
+    b.close()
+    assert total > 100 and near <= 0.01 * total, f"{near} near-boundary draws of {total}"
