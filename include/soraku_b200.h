@@ -149,6 +149,9 @@ int skb_decode_attention(const float *qkv, int rows, int n_heads, int n_kv_heads
  * stream capture.  All calls share the array and it keeps the last call's
  * contents: calls that overlap on the GPU (different streams, or different
  * host threads on one device) race and must be serialised by the caller.
+ * Every argument is checked before the array is touched.  The looked-up
+ * address is cached per device and goes stale after cudaDeviceReset on that
+ * device: do not call this entry point on a device after resetting it.
  * No cudaMalloc, cudaFree or allocating library routine is called. */
 #define SKB_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u + 1024u)
 int skb_decode_attention_noalloc(const float *qkv, int rows, int n_heads, int n_kv_heads,
@@ -167,6 +170,11 @@ int skb_test_exp(const float *x, float *y, int n, cudaStream_t stream);
 int skb_test_gemm(const float *x, const float *w, float *out, int M, int N, int K, int tensor_cores, int splits,
                   cudaStream_t stream);
 int skb_test_philox(const uint32_t *ctr_key, uint32_t *out, int n, cudaStream_t stream);
+/* Failure-path hook: a one-thread kernel waits limit_us (1..10^6) on an
+ * mbarrier phase nothing completes, through the decode kernels' bounded wait,
+ * which gives up and sets *err (device int); the call synchronises `stream`
+ * and returns SKB_ERR_CUDA when the flag is set, SKB_OK otherwise. */
+int skb_test_wait_timeout(int *err, int limit_us, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------
  * Decode engine: replaces GraphFrameEngine (graph_frame.py:23-328).
@@ -265,7 +273,13 @@ int skb_engine_set_sampling(skb_engine *eng, int request, float cfg_scale, float
 int skb_engine_capture(skb_engine *eng, int n_active, int frames_per_graph, cudaStream_t stream);
 
 /* graph_frame.py:298-305 step_frame: replays the graph once (frames_per_graph
- * frames).  mask_eos_q0 is the host EOS flag of eos_rule 0. */
+ * frames).  mask_eos_q0 is the host EOS flag of eos_rule 0.  Device error
+ * flags (view 6: a position out of range, a prefill input out of range, a
+ * weight copy that did not arrive within its bounded wait) surface here as
+ * SKB_ERR_CUDA: each step queues a copy of the flags behind its replay, and
+ * a later step reports a raised flag once that copy has landed (without
+ * waiting for it); after that every step fails, as graph_frame.py:155-156,
+ * 301-302 raise RuntimeError for an unusable engine. */
 int skb_engine_step(skb_engine *eng, int mask_eos_q0, cudaStream_t stream);
 
 /* Runs the same frame body eagerly (kernel by kernel, no graph). */
@@ -284,7 +298,8 @@ int skb_engine_frames(skb_engine *eng, int request);
  * q) under its seed; default: the slot index), so a request's draws need not
  * depend on the slot it occupies.
  * status: device frame counters and EOS flags of requests [0, n) into host
- * arrays (synchronises the stream).
+ * arrays (synchronises the stream); returns SKB_ERR_CUDA if a device error
+ * flag is raised.
  * move_request: moves request `src`'s decode state (sampling state, codes,
  * prefix, residual stream, positions, KV pages by page-table exchange) into
  * slot `dst`, leaving `src` free; for compacting the active slots. */

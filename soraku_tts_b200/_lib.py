@@ -41,6 +41,7 @@ SIGNATURES = {
                                              c_int, c_int, c_void_p, c_void_p]),
     "skb_test_exp": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "skb_test_philox": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "skb_test_wait_timeout": (c_int, [c_void_p, c_int, c_void_p]),
     "skb_test_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "skb_engine_create": (c_int, [c_void_p, c_void_p, c_void_p]),
     "skb_engine_destroy": (c_int, [c_void_p]),

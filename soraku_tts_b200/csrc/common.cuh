@@ -172,10 +172,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// Waits for phase `parity` of an mbarrier, giving up after ~2 s: then it
-// records the failure in *err (if given) and returns false, so a kernel never
-// hangs on a copy that does not arrive.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Waits for phase `parity` of an mbarrier, giving up after `limit_ns`: then
+// it records the failure in *err (if given) and returns false, so a kernel
+// never hangs on a copy that does not arrive.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err, uint64_t limit_ns) {
     const uint32_t addr = smem_u32(bar);
     uint64_t t0 = 0;
     for (int it = 0;; ++it) {
@@ -187,11 +187,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
             : "memory");
         if (done) return true;
         if (it == 0) t0 = globaltimer_ns();
-        else if ((it & 255) == 0 && globaltimer_ns() - t0 > 2000000000ull) {
+        else if ((it & 255) == 0 && globaltimer_ns() - t0 > limit_ns) {
             if (err) atomicExch(err, 1);
             return false;
         }
     }
+}
+// The decode kernels' wait: about 2 s.
+constexpr uint64_t SKB_WAIT_LIMIT_NS = 2000000000ull;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    return mbar_wait_limit(bar, parity, err, SKB_WAIT_LIMIT_NS);
 }
 
 // --------------------------------------------------------- kernel stamps

@@ -106,6 +106,12 @@ struct skb_engine {
     std::vector<int> frames_host, pos_host;
     std::vector<ReqState> st_host;
     std::vector<void*> allocs;
+    // device error flags seen from the host: each step queues a copy of the
+    // flags into pinned memory; a later step checks it once it has landed
+    int* err_host = nullptr;
+    cudaEvent_t err_ev = nullptr;
+    bool err_pending = false;
+    int err_seen = -1;  // index of the first raised flag observed (sticky)
 };
 
 namespace {
@@ -421,6 +427,13 @@ void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& n
     }
 }
 
+// The frame's kernel list for a batch of n_active requests.  A captured graph
+// bakes in, besides n_active and frames per replay (its cache key), engine
+// state fixed at creation: the buffers and weight pointers, gemm_min_rows,
+// attn_variant, the attention split count S, the opts' use_pdl and
+// l2_prefetch, and the debug flag.  skb_engine_set_debug drops every cached
+// graph when the flag changes; any future setter of the other state must do
+// the same (destroy_graph) or add that state to CachedGraph's key.
 std::vector<Node> build_frame(skb_engine* e, int n_active) {
     const int R = n_active * e->rpr;
     std::vector<Node> nodes;
@@ -682,6 +695,13 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
         s.eos_rule = 0;
     }
     cudaMemcpy(e->st, e->st_host.data(), sizeof(ReqState) * e->nreq, cudaMemcpyHostToDevice);
+    if (cudaHostAlloc(reinterpret_cast<void**>(&e->err_host), 8 * sizeof(int), cudaHostAllocDefault) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->err_ev, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        skb_engine_destroy(e);
+        return fail(SKB_ERR_CUDA, "engine_create: error-flag mirror");
+    }
+    memset(e->err_host, 0, 8 * sizeof(int));
     if (cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
         skb_engine_destroy(e);
         return fail(SKB_ERR_CUDA, "stream creation failed");
@@ -705,6 +725,8 @@ int skb_engine_destroy(skb_engine* e) {
     if (!e) return SKB_OK;
     destroy_graph(e);
     if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
+    if (e->err_ev) cudaEventDestroy(e->err_ev);
+    if (e->err_host) cudaFreeHost(e->err_host);
     for (void* p : e->allocs) cudaFree(p);
     delete e;
     return SKB_OK;
@@ -1032,16 +1054,57 @@ static void advance_host(skb_engine* e, int n_active, int frames) {
     }
 }
 
+// Device error flags: 0 a position out of range (attention), 1 a prefill
+// token id or code out of range, 2 a weight copy that did not arrive in time
+// (GEMV / tensor-core GEMM).  Once a flag has been observed every later step
+// fails: the engine's state can no longer be trusted.
+static const char* const kFlagWhat[8] = {"position out of range", "prefill input out of range",
+                                         "a weight copy did not arrive in time", "flag 3", "flag 4", "flag 5",
+                                         "flag 6", "flag 7"};
+static int flag_status(skb_engine* e) {
+    if (e->err_seen < 0) {
+        for (int i = 0; i < 8; ++i)
+            if (e->err_host[i] != 0) {
+                e->err_seen = i;
+                break;
+            }
+    }
+    if (e->err_seen >= 0)
+        return fail(SKB_ERR_CUDA, "device error flag %d raised by an earlier launch (%s)", e->err_seen,
+                    kFlagWhat[e->err_seen]);
+    return SKB_OK;
+}
+
+// Checks the flags copied by an earlier step, without waiting for the copy.
+static int check_flags_async(skb_engine* e) {
+    if (e->err_pending && cudaEventQuery(e->err_ev) == cudaSuccess) e->err_pending = false;
+    if (e->err_pending) return e->err_seen >= 0 ? flag_status(e) : SKB_OK;
+    return flag_status(e);
+}
+
+// Queues a copy of the device flags behind the work already on `stream`.
+static void queue_flag_copy(skb_engine* e, cudaStream_t stream) {
+    if (e->err_pending) return;
+    if (cudaMemcpyAsync(e->err_host, e->err, 8 * sizeof(int), cudaMemcpyDeviceToHost, stream) == cudaSuccess &&
+        cudaEventRecord(e->err_ev, stream) == cudaSuccess)
+        e->err_pending = true;
+    else
+        cudaGetLastError();
+}
+
 int skb_engine_step(skb_engine* e, int mask_eos_q0, cudaStream_t stream) {
     if (!e) return fail(SKB_ERR_ARG, "step: null engine");
     if (!e->exec) return fail(SKB_ERR_STATE, "call capture() first");
-    int st = check_capacity(e, e->graph_active, e->graph_fpg);
+    int st = check_flags_async(e);
+    if (st) return st;
+    st = check_capacity(e, e->graph_active, e->graph_fpg);
     if (st) return st;
     static thread_local int flag_val;
     flag_val = mask_eos_q0 ? 1 : 0;
     cudaError_t err = cudaMemcpyAsync(e->host_flag, &flag_val, sizeof(int), cudaMemcpyHostToDevice, stream);
     if (err == cudaSuccess) err = cudaGraphLaunch(e->exec, stream);
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "step: %s", cudaGetErrorString(err));
+    queue_flag_copy(e, stream);
     advance_host(e, e->graph_active, e->graph_fpg);
     return SKB_OK;
 }
@@ -1105,7 +1168,12 @@ int skb_engine_status(skb_engine* e, int n, int32_t* frames, int32_t* done, cuda
     std::vector<ReqState> tmp(n);
     cudaError_t err = cudaMemcpyAsync(tmp.data(), e->st, sizeof(ReqState) * n, cudaMemcpyDeviceToHost, s);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err == cudaSuccess && e->err_pending) err = cudaEventSynchronize(e->err_ev);
+    e->err_pending = false;
+    if (err == cudaSuccess) err = cudaMemcpy(e->err_host, e->err, 8 * sizeof(int), cudaMemcpyDeviceToHost);
     if (err != cudaSuccess) return fail(SKB_ERR_CUDA, "status: %s", cudaGetErrorString(err));
+    const int fst = flag_status(e);
+    if (fst) return fst;
     for (int r = 0; r < n; ++r) {
         frames[r] = tmp[r].frame;
         done[r] = tmp[r].done;

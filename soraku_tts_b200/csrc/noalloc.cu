@@ -8,10 +8,13 @@
 // would fault, or read the wrong memory.  So the first call on each device
 // looks the device address up with cudaGetSymbolAddress while that device is
 // current, checks the result and caches it; every launch receives that looked-up
-// pointer.  Every call reuses the array, which keeps the previous call's
-// contents: the tickets, which must start at zero, are cleared with
-// cudaMemsetAsync on the caller's stream before each launch.  Calls that
-// overlap on the GPU share the array and therefore race.
+// pointer.  The cached address belongs to the device's current context: after
+// cudaDeviceReset on that device it is stale, so a program that resets a
+// device must not call this entry point on it again.  Every call reuses the
+// array, which keeps the previous call's contents: the tickets, which must
+// start at zero, are cleared with cudaMemsetAsync on the caller's stream
+// before each launch (after every argument check).  Calls that overlap on the
+// GPU share the array and therefore race.
 #include <mutex>
 
 #include "ops.cuh"
@@ -26,6 +29,10 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocTicketB
 
 namespace skb {
 
+int decode_attention_check(const float* qkv, int rows, int H, int KVH, int hd, const float* qn, const float* kn,
+                           const float* rc, const float* rs, int max_len, const int32_t* pos, const float* kv_pool,
+                           const int32_t* page_table, int max_pages, int page_size, int n_pages, int splits,
+                           const float* out);
 int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, const float* qn, const float* kn,
                         float eps, const float* rc, const float* rs, int max_len, const int32_t* pos, float* kv_pool,
                         const int32_t* page_table, int max_pages, int page_size, int n_pages, int splits,
@@ -78,6 +85,12 @@ extern "C" int skb_decode_attention_noalloc(const float* qkv, int rows, int n_he
                     "decode_attention_noalloc: rows %d x kv heads %d x splits %d needs %llu bytes of partials "
                     "and %llu of tickets; the built-in scratch holds %zu and %zu",
                     rows, n_kv_heads, splits, part_floats * 4, tickets * 4, kNoallocPartBytes, kNoallocTicketBytes);
+    // every argument is checked before the shared array is touched, so a
+    // rejected call never disturbs a call still running on another stream
+    const int chk = decode_attention_check(qkv, rows, n_heads, n_kv_heads, head_dim, q_norm, k_norm, rope_cos,
+                                           rope_sin, max_len, pos, kv_pool, page_table, max_pages, page_size,
+                                           n_pages, splits, out);
+    if (chk != SKB_OK) return chk;
     unsigned char* scratch = nullptr;
     const int st = scratch_for_current_device(&scratch);
     if (st != SKB_OK) return st;

@@ -292,6 +292,19 @@ GemvArgs gemv_args_plain(const float* x, int ldx, int N, int K) {
     return a;
 }
 
+// Failure-path hook: one thread waits, with a short limit, on an mbarrier
+// phase that nothing completes (no copy is in flight), through the same
+// bounded wait the decode kernels use; the wait gives up, sets *err and the
+// kernel returns, leaving the context usable.
+__global__ void test_wait_timeout_kernel(int* err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        mbar_wait_limit(&bar, 0u, err, limit_ns);
+    }
+}
+
 }  // namespace skb
 
 using namespace skb;
@@ -413,6 +426,19 @@ int skb_test_exp(const float* x, float* y, int n, cudaStream_t stream) {
     if (n == 0) return SKB_OK;
     test_exp_kernel<<<(n + 255) / 256, 256, 0, stream>>>(x, y, n);
     return check_launch("test_exp");
+}
+
+int skb_test_wait_timeout(int* err, int limit_us, cudaStream_t stream) {
+    if (!err || limit_us < 1 || limit_us > 1000000) return fail(SKB_ERR_ARG, "test_wait_timeout: bad arguments");
+    test_wait_timeout_kernel<<<1, 32, 0, stream>>>(err, (unsigned long long)limit_us * 1000ull);
+    int st = check_launch("test_wait_timeout");
+    if (st != SKB_OK) return st;
+    cudaError_t e = cudaStreamSynchronize(stream);
+    int flag = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&flag, err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail(SKB_ERR_CUDA, "test_wait_timeout: %s", cudaGetErrorString(e));
+    if (flag != 0) return fail(SKB_ERR_CUDA, "a device wait gave up after %d us and raised its error flag", limit_us);
+    return SKB_OK;
 }
 
 int skb_test_philox(const uint32_t* ctr_key, uint32_t* out, int n, cudaStream_t stream) {

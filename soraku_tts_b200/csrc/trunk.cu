@@ -399,11 +399,12 @@ cudaError_t gather_rows_launch(const float* X, const int* src, const int* dst, i
     return launch(gather_rows_kernel, dim3(n), dim3(256), 0, s, false, X, src, dst, out, D);
 }
 
-int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, const float* qn, const float* kn,
-                        float eps, const float* rc, const float* rs, int max_len, const int32_t* pos, float* kv_pool,
-                        const int32_t* page_table, int max_pages, int page_size, int n_pages, int splits,
-                        float* part, int32_t* tickets, float* out, cudaStream_t stream) {
-    if (!qkv || !qn || !kn || !rc || !rs || !pos || !kv_pool || !page_table || !part || !tickets || !out)
+// Argument checks of the decode-attention op (every pointer but the scratch).
+int decode_attention_check(const float* qkv, int rows, int H, int KVH, int hd, const float* qn, const float* kn,
+                           const float* rc, const float* rs, int max_len, const int32_t* pos, const float* kv_pool,
+                           const int32_t* page_table, int max_pages, int page_size, int n_pages, int splits,
+                           const float* out) {
+    if (!qkv || !qn || !kn || !rc || !rs || !pos || !kv_pool || !page_table || !out)
         return fail(SKB_ERR_ARG, "decode_attention: null pointer");
     if (hd != 128 || KVH < 1 || H % KVH != 0 || H / KVH > 2)
         return fail(SKB_ERR_ARG, "decode_attention: head_dim must be 128 and heads/kv_heads 1 or 2");
@@ -411,6 +412,17 @@ int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, cons
         return fail(SKB_ERR_ARG, "decode_attention: bad sizes");
     if (page_size < 1 || (page_size & (page_size - 1)) != 0 || (long long)max_pages * page_size < max_len)
         return fail(SKB_ERR_ARG, "decode_attention: page_size must be a power of two covering max_len");
+    return SKB_OK;
+}
+
+int decode_attention_op(const float* qkv, int rows, int H, int KVH, int hd, const float* qn, const float* kn,
+                        float eps, const float* rc, const float* rs, int max_len, const int32_t* pos, float* kv_pool,
+                        const int32_t* page_table, int max_pages, int page_size, int n_pages, int splits,
+                        float* part, int32_t* tickets, float* out, cudaStream_t stream) {
+    const int chk = decode_attention_check(qkv, rows, H, KVH, hd, qn, kn, rc, rs, max_len, pos, kv_pool, page_table,
+                                           max_pages, page_size, n_pages, splits, out);
+    if (chk != SKB_OK) return chk;
+    if (!part || !tickets) return fail(SKB_ERR_ARG, "decode_attention: null scratch pointer");
     DecodeAttnArgs a = {};
     a.qkv = qkv;
     a.ld_qkv = (H + 2 * KVH) * hd;

@@ -43,3 +43,17 @@ def test_reference_arm_other_ranks_exit_quietly():
     res = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert res.returncode == 0
     assert not any(ln.strip().startswith("{") for ln in res.stdout.splitlines())
+
+
+def test_reference_arm_config4():
+    """--impl reference --workload config4 samples three of the ragged requests."""
+    env = dict(os.environ)
+    res = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--workload",
+                          "config4", "--steps", "1", "--warmup", "0", "--cpu-frames", "1"], cwd=REPO, env=env,
+                         capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [ln for ln in res.stdout.splitlines() if ln.strip().startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["config"]["workload"] == "config4"
+    assert "config4 requests" in d["cpu_baseline"]["sample"]

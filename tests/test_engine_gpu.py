@@ -315,3 +315,28 @@ def test_full_model_route_d_config3(full_route_d):
     codes, logits, hidden0 = _decode(model, data, 8, seed=31, speaker=spk)
     assert_close(hidden0, data["hidden"][0], what="route-D full prefill hidden (vs reference golden)", **TOL)
     _check_frames(orc, data, meta, codes, logits, temperature=0.9, top_k=50, top_p=0.95, seed=31, speaker=spk)
+
+
+def test_fast_generator_streams_on_frame(small):
+    """generate(on_frame=...) hands each emitted frame to the callback as
+    int64 [1, 1, 16], in order, equal to the returned codes, as the
+    reference's streaming hook does (fast_generate.py:459-460, 555-556)."""
+    from soraku_tts_b200.fast_generate import FastGenerator
+
+    data, meta, orc, model = small
+    gen = FastGenerator(model, device=torch.device("cuda"), frames_per_graph=4)
+    got = []
+    kw = dict(max_new_frames=6, min_new_frames=6, temperature=0.9, top_k=50, top_p=0.95, cfg_scale=1.5, seed=77)
+    codes, info = gen.generate(input_ids=torch.from_numpy(data["input_ids"]),
+                               prompt_codes=torch.from_numpy(data["prompt_codes"]),
+                               uncond_input_ids=torch.from_numpy(data["uncond_input_ids"]),
+                               on_frame=lambda f: got.append(f.clone()), **kw)
+    assert info["num_frames"] == 6 and len(got) == 6
+    for i, f in enumerate(got):
+        assert tuple(f.shape) == (1, 1, 16) and f.dtype == torch.int64
+        np.testing.assert_array_equal(f.view(16).cpu().numpy(), codes[i].cpu().numpy())
+    # the streamed run draws the same codes as a chunked run without the hook
+    codes2, _ = gen.generate(input_ids=torch.from_numpy(data["input_ids"]),
+                             prompt_codes=torch.from_numpy(data["prompt_codes"]),
+                             uncond_input_ids=torch.from_numpy(data["uncond_input_ids"]), **kw)
+    np.testing.assert_array_equal(codes.numpy(), codes2.numpy())

@@ -84,3 +84,29 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
                                                  8, P, 16, 64, 1, None)
     assert st == _lib.SKB_ERR_ARG
     assert "scratch" in _lib.last_error()
+
+
+def test_noalloc_at_its_exact_partials_limit():
+    """2 rows x 8 kv heads x 2 heads per group x 130 floats: 126 splits need
+    2,096,640 bytes of partials (the largest count within the 2 MiB array) and
+    must match the allocating entry point; 127 splits (2,113,280 bytes) must be
+    refused."""
+    from soraku_tts_b200 import _lib
+
+    c = _case(12)
+    pos = torch.tensor([300, 129], dtype=torch.int32, device="cuda")
+    qkv = torch.from_numpy(c["g"].standard_normal((c["rows"], (H + 2 * KVH) * HD)).astype(np.float32)).cuda()
+    splits = 126
+    assert c["rows"] * KVH * splits * (H // KVH) * (HD + 2) * 4 <= 2 * 1024 * 1024
+    part = torch.empty(c["rows"] * KVH * splits * (H // KVH) * (HD + 2), dtype=torch.float32, device="cuda")
+    tickets = torch.zeros(c["rows"] * KVH, dtype=torch.int32, device="cuda")
+    pool_a, pool_b = c["pool"].clone(), c["pool"].clone()
+    out_a = torch.empty((c["rows"], H * HD), device="cuda")
+    out_b = torch.full((c["rows"], H * HD), float("nan"), device="cuda")
+    _call(_lib, "skb_decode_attention", c, qkv, pos, pool_a, splits, out_a, scratch=(part, tickets))
+    _call(_lib, "skb_decode_attention_noalloc", c, qkv, pos, pool_b, splits, out_b)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out_b.cpu().numpy(), out_a.cpu().numpy(), **TOL)
+    np.testing.assert_allclose(pool_b.cpu().numpy(), pool_a.cpu().numpy(), **TOL)
+    with pytest.raises(ValueError, match="scratch"):  # SKB_ERR_ARG
+        _call(_lib, "skb_decode_attention_noalloc", c, qkv, pos, pool_b, splits + 1, out_b)
