@@ -234,6 +234,11 @@ typedef struct {
                              per layer, mapped to rows by
                              skb_engine_map_pages (unmapped positions are
                              refused by prefill and step)                   */
+    int split_depth_head; /* 0: a batch of one CFG request on the GEMV path
+                             runs the frame's 16 depth steps as one
+                             persistent cooperative launch (gate/up slices
+                             resident in shared memory, grid barriers
+                             between phases); 1: 64 separate kernels    */
 } skb_engine_opts;
 
 int skb_engine_create(const skb_model_desc *model, const skb_engine_opts *opts, skb_engine **out);
@@ -320,7 +325,10 @@ int skb_engine_map_pages(skb_engine *eng, int row, int first, int n, const int32
  * frame with debug on: earliest CTA start, earliest and latest release from
  * the dependent-launch wait, latest CTA end, then the latest CTA to reach
  * kernel-specific points (%globaltimer ns; the caller resets it to
- * {max, max, 0, ...} before the frame). */
+ * {max, max, 0, ...} before the frame); 9 persistent depth-head timeline
+ * uint64 [4 Q][2] of the last frame with debug on (CTA 0's release of each
+ * phase -- UP, DN, CLS, SAMPLE per codebook -- and the end of its work,
+ * %globaltimer ns). */
 int skb_engine_view(skb_engine *eng, int which, void **ptr, int64_t *numel);
 
 /* Keep the per-(q) logits of the last frame in the history buffer (view 4). */

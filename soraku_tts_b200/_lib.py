@@ -93,7 +93,8 @@ class skb_engine_opts(ctypes.Structure):
     _fields_ = [("max_requests", c_int), ("rows_per_request", c_int), ("max_len", c_int),
                 ("max_frames", c_int), ("max_prefill", c_int), ("page_size", c_int),
                 ("attn_splits", c_int), ("use_pdl", c_int), ("l2_prefetch", c_int), ("gemm_min_rows", c_int),
-                ("prefill_batch", c_int), ("kv_pages", c_int)]
+                ("prefill_batch", c_int), ("kv_pages", c_int),
+                ("split_depth_head", c_int)]
 
 
 _lib = None

@@ -26,6 +26,7 @@
 #include <functional>
 #include <vector>
 
+#include "depth_head.cuh"
 #include "engine_types.cuh"
 #include "trunk.cuh"
 #include "ops.cuh"
@@ -108,6 +109,11 @@ struct skb_engine {
     std::vector<void*> allocs;
     // device error flags seen from the host: each step queues a copy of the
     // flags into pinned memory; a later step checks it once it has landed
+    // persistent depth head (depth_head.cu) for a batch of one CFG request
+    bool dh_ok = false;
+    unsigned* dh_bar = nullptr;  // its grid barrier word
+    int* dh_abort = nullptr;
+    unsigned long long* dh_ts = nullptr;  // debug phase timeline [4 Q][2]
     int* err_host = nullptr;
     cudaEvent_t err_ev = nullptr;
     bool err_pending = false;
@@ -441,7 +447,54 @@ std::vector<Node> build_frame(skb_engine* e, int n_active) {
     auto stamps = [e, &nodes, R]() {
         return (e->debug && R < e->gemm_min_rows) ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr;
     };
-    for (const Phase& ph : build_phases(e, n_active)) {
+    const std::vector<Phase> phases = build_phases(e, n_active);
+    size_t first = 0;
+    if (R == 2 && e->dh_ok) {
+        // one CFG request on the GEMV path: the 16 depth steps as one
+        // persistent cooperative launch (its phases are the first 3 Q)
+        DepthArgs da = {};
+        da.V = e->V;
+        da.Q = e->Q;
+        da.rms_eps = e->m.rms_eps;
+        da.depth_eps = e->m.depth_eps;
+        da.scale = e->m.frame_scale;
+        da.final_norm = e->m.final_norm;
+        da.norm_in = e->m.depth_norm_in;
+        da.norm_out = e->m.depth_norm_out;
+        da.wg = e->m.depth_gate;
+        da.wu = e->m.depth_up;
+        da.wd = e->m.depth_down;
+        da.table = e->m.table;
+        da.bias = e->m.depth_bias;
+        da.x = e->x;
+        da.act = e->act;
+        da.y = e->y;
+        da.hidden = e->hidden;
+        da.logits = e->debug ? e->logits_hist : e->logits;
+        da.logits_q_stride = e->debug ? e->R * e->V : 0;
+        da.st = e->st;
+        da.host_flag = e->host_flag;
+        da.cur_codes = e->cur_codes;
+        da.hist = e->hist;
+        da.max_frames = e->o.max_frames;
+        da.bos = e->m.bos_id;
+        da.pad = e->m.pad_id;
+        da.eos = e->m.eos_id;
+        da.bar = e->dh_bar;
+        da.abort = e->dh_abort;
+        da.err = e->err;
+        da.ts = e->debug ? e->dh_ts : nullptr;
+        const int grid = e->nsm;
+        Node n;
+        n.w.push_back({(const char*)e->m.depth_gate, (unsigned long long)e->I * e->D * 4});
+        n.w.push_back({(const char*)e->m.depth_up, (unsigned long long)e->I * e->D * 4});
+        n.ctas = grid;
+        n.run = [da, grid](cudaStream_t s, bool, const PrefetchList&) { return depth_head_launch(da, grid, s); };
+        nodes.push_back(n);
+        first = (size_t)3 * e->Q;
+    }
+    for (size_t pi = first; pi < phases.size(); ++pi) {
+        const Phase& ph = phases[pi];
         if (ph.kind == PH_GEMV) {
             GemvArgs g = ph.g;
             g.ts = stamps();
@@ -657,6 +710,9 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->ptok, T)
     A(e->pframes, (size_t)e->prefill_batch * (opts->max_prefill + 1) * e->Q)
     A(e->pmeta, (size_t)5 * e->prefill_batch * e->rpr)
+    A(e->dh_bar, 1)
+    A(e->dh_abort, 1)
+    A(e->dh_ts, (size_t)2 * depth_head_phases(e->Q))
 #undef A
     if (st != SKB_OK) {
         skb_engine_destroy(e);
@@ -695,6 +751,8 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
         s.eos_rule = 0;
     }
     cudaMemcpy(e->st, e->st_host.data(), sizeof(ReqState) * e->nreq, cudaMemcpyHostToDevice);
+    e->dh_ok = e->rpr == 2 && !opts->split_depth_head && e->gemm_min_rows > 2 &&
+               depth_head_supported(e->D, e->I, e->V, e->Q, e->nsm, e->device);
     if (cudaHostAlloc(reinterpret_cast<void**>(&e->err_host), 8 * sizeof(int), cudaHostAllocDefault) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->err_ev, cudaEventDisableTiming) != cudaSuccess) {
         cudaGetLastError();
@@ -709,6 +767,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     set_smem_attrs(depth_sample_kernel<DEPTH_VMAX_SMALL>, sampler_smem_bytes<DEPTH_VMAX_SMALL>());
     set_smem_attrs(depth_sample_kernel<SAMPLER_VMAX>, sampler_smem_bytes<SAMPLER_VMAX>());
     decode_attn_cluster_prepare();
+    depth_head_prepare();
     trunk_init_attrs();
     gemv_prepare_all();
     tgemm_prepare();
@@ -1223,6 +1282,7 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
         case 8: *ptr = e->kts; *numel = (int64_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5); break;
+        case 9: *ptr = e->dh_ts; *numel = (int64_t)2 * depth_head_phases(e->Q); break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }
     return SKB_OK;

@@ -30,6 +30,7 @@ cudaError_t prefill_attn_launch(const float* Q, const int* row_off, const int* r
                                 const KVLayout& kv, int layer, float scale, float* out,
                                 cudaStream_t s);
 cudaError_t trunk_init_attrs();
+
 cudaError_t gather_rows_launch(const float* X, const int* src, const int* dst, int n, float* out,
                                int D, cudaStream_t s);
 

@@ -42,12 +42,13 @@ class NativeEngine:
 
     def __init__(self, model, *, max_requests=1, rows_per_request=2, max_len=1024, max_frames=1024,
                  max_prefill=None, page_size=64, attn_splits=0, use_pdl=True, l2_prefetch=True, gemm_min_rows=0,
-                 prefill_batch=1, kv_pages=0):
+                 prefill_batch=1, kv_pages=0, split_depth_head=False):
         self.model = model
         opts = _lib.skb_engine_opts(max_requests, rows_per_request, max_len, max_frames,
                                     max_prefill if max_prefill else max_len, page_size, attn_splits,
                                     1 if use_pdl else 0, 1 if l2_prefetch else 0, int(gemm_min_rows),
-                                    int(prefill_batch), int(kv_pages))
+                                    int(prefill_batch), int(kv_pages),
+                                    1 if split_depth_head else 0)
         self.prefill_batch = max(1, int(prefill_batch))
         self.page_size = page_size
         handle = ctypes.c_void_p()

@@ -340,3 +340,11 @@ def test_fast_generator_streams_on_frame(small):
                              prompt_codes=torch.from_numpy(data["prompt_codes"]),
                              uncond_input_ids=torch.from_numpy(data["uncond_input_ids"]), **kw)
     np.testing.assert_array_equal(codes.numpy(), codes2.numpy())
+
+
+def test_separate_depth_kernels_match_oracle(small):
+    """The frame's depth head as 64 separate kernels (the path batched rows
+    take) against the oracle, like the default persistent depth head."""
+    data, meta, orc, model = small
+    codes, logits, _ = _decode(model, data, 3, seed=404, split_depth_head=True)
+    _check_frames(orc, data, meta, codes, logits, temperature=0.9, top_k=50, top_p=0.95, seed=404)
