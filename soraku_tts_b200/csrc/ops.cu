@@ -9,6 +9,7 @@
 #include "gemv.cuh"
 #include "ops.cuh"
 #include "sampler.cuh"
+#include "trunk_api.cuh"
 
 namespace skb {
 
@@ -262,6 +263,32 @@ int cfg_sample(const float* logits, int rows_per_req, int n_req, int V,
 // B rows are processed in blocks of at most 4 (the register-resident
 // activation tile of gemv_kernel).
 static int gemv_rows(GemvArgs a, int B, int XM, int EM, cudaStream_t s, const char* what) {
+    // more than 4 rows: one pass of the 3xTF32 tensor-core GEMM over all of
+    // them (the weights are read once), where its tiling accepts the shape
+    if (B > 4 && XM == X_PLAIN && a.K % 32 == 0) {
+        GemmArgs g = {};
+        g.A = a.x;
+        g.lda = a.ldx;
+        g.w0 = a.w0;
+        g.w1 = a.w1;
+        g.w2 = a.w2;
+        g.seg1 = a.seg1;
+        g.seg2 = a.seg2;
+        g.interleave = a.interleave;
+        g.N = a.N;
+        g.K = a.K;
+        g.T = B;
+        g.out = a.out;
+        g.ldo = a.ldo;
+        g.resid = a.resid;
+        g.ldr = a.ldr;
+        g.bias = a.bias;
+        g.mode = EM == E_RESID ? 1 : (EM == E_BIAS ? 2 : (EM == E_SWIGLU ? 3 : 0));
+        const cudaError_t e = tgemm_launch(g, s, false);
+        if (e == cudaSuccess) return SKB_OK;
+        if (e != cudaErrorInvalidValue) return fail(SKB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+        cudaGetLastError();  // a shape the tiling does not take: the ring GEMV below
+    }
     int grid = a.N / (EM == E_SWIGLU ? 2 : 1);
     if (grid > 148) grid = 148;
     if (grid < 1) grid = 1;
