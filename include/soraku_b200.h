@@ -165,8 +165,11 @@ int skb_decode_attention_noalloc(const float *qkv, int rows, int n_heads, int n_
  * ctr_key: device uint32 [n, 6] = (c0, c1, c2, c3, k0, k1); out: [n, 4]. */
 int skb_test_exp(const float *x, float *y, int n, cudaStream_t stream);
 /* out[M, N] = x[M, K] @ w[N, K]^T on the batched/prefill GEMM: tensor_cores
- * 1 = the 3xTF32 tcgen05 kernel (splits: K splits per output tile, 0 =
- * chosen by occupancy), 0 = the SIMT FP32 kernel.  K % 32 == 0. */
+ * 1 = the kernel chosen by M (the FP32 FFMA few-row kernel for M <= 16 and
+ * K % 256 == 0, else the 3xTF32 tcgen05 kernel), 2 = the tcgen05 kernel,
+ * 3 = the FFMA few-row kernel (M <= 32, K % 256 == 0); splits: K splits per
+ * tcgen05 output tile, 0 = chosen by occupancy; 0 = the SIMT FP32 prefill
+ * kernel.  K % 32 == 0. */
 int skb_test_gemm(const float *x, const float *w, float *out, int M, int N, int K, int tensor_cores, int splits,
                   cudaStream_t stream);
 int skb_test_philox(const uint32_t *ctr_key, uint32_t *out, int n, cudaStream_t stream);

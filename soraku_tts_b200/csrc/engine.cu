@@ -221,6 +221,14 @@ Phase gemv_phase(const GemvArgs& a, int XM, int EM) {
 
 // The frame as a program of phases (16 depth steps, then the trunk layers),
 // turned into kernel launches chained with PDL by build_frame.
+// Debug timeline blocks: at most 6 launches per depth step (norm + GEMM for
+// up and classifier, down, sampler), 7 per layer (norm + GEMM for QKV and
+// gate/up, attention, O, down) and the position advance.
+int kts_slots(const skb_engine* e) { return e->Q * 6 + e->L * 7 + 1; }
+unsigned long long* node_stamps(const skb_engine* e, size_t node) {
+    return (e->debug && (int)node < kts_slots(e)) ? e->kts + SKB_KTS_STRIDE * node : nullptr;
+}
+
 std::vector<Phase> build_phases(skb_engine* e, int n_active) {
     std::vector<Phase> phases;
     const int R = n_active * e->rpr;
@@ -390,6 +398,7 @@ void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& n
         na.hout = g.hout;
         na.D = g.K;
         na.mode = ph.xm == X_NORM_ADD_NORM ? 3 : 1;
+        na.ts = node_stamps(e, nodes.size());
         Node n;
         n.ctas = R;
         n.run = [na, R](cudaStream_t s, bool pdl, const PrefetchList&) {
@@ -416,6 +425,7 @@ void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& n
     a.bias = g.bias;
     a.mode = ph.em == E_RESID ? 1 : (ph.em == E_BIAS ? 2 : (ph.em == E_SWIGLU ? 3 : 0));
     a.err = e->err + 2;
+    a.ts = node_stamps(e, nodes.size());
     Node n;
     n.w = gemv_ranges(g);
     n.ctas = ((a.N + 63) / 64) * ((R + 127) / 128);
@@ -443,10 +453,8 @@ void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& n
 std::vector<Node> build_frame(skb_engine* e, int n_active) {
     const int R = n_active * e->rpr;
     std::vector<Node> nodes;
-    // debug timeline: the ring-GEMV frame only (its kernel count is what kts holds)
-    auto stamps = [e, &nodes, R]() {
-        return (e->debug && R < e->gemm_min_rows) ? e->kts + SKB_KTS_STRIDE * nodes.size() : nullptr;
-    };
+    // debug timeline: one stamp block per launch of the frame
+    auto stamps = [e, &nodes]() { return node_stamps(e, nodes.size()); };
     const std::vector<Phase> phases = build_phases(e, n_active);
     size_t first = 0;
     if (R == 2 && e->dh_ok) {
@@ -692,7 +700,7 @@ int skb_engine_create(const skb_model_desc* md, const skb_engine_opts* opts, skb
     A(e->pos, e->R)
     A(e->page_table, (size_t)e->R * e->max_pages)
     A(e->err, 8)
-    A(e->kts, (size_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5))
+    A(e->kts, (size_t)SKB_KTS_STRIDE * kts_slots(e))
     if (e->R >= e->gemm_min_rows) A(e->xn, (size_t)e->R * 3072)
     A(e->pt_tmp, (size_t)e->max_pages)
     A(e->host_flag, 1)
@@ -1281,7 +1289,7 @@ int skb_engine_view(skb_engine* e, int which, void** ptr, int64_t* numel) {
         case 5: *ptr = e->prefix; *numel = (int64_t)e->nreq * e->D; break;
         case 6: *ptr = e->err; *numel = 8; break;
         case 7: *ptr = e->st; *numel = (int64_t)e->nreq * (int64_t)(sizeof(ReqState) / 4); break;
-        case 8: *ptr = e->kts; *numel = (int64_t)SKB_KTS_STRIDE * (e->Q * 4 + e->L * 5); break;
+        case 8: *ptr = e->kts; *numel = (int64_t)SKB_KTS_STRIDE * kts_slots(e); break;
         case 9: *ptr = e->dh_ts; *numel = (int64_t)2 * depth_head_phases(e->Q); break;
         default: return fail(SKB_ERR_ARG, "view: unknown buffer %d", which);
     }

@@ -71,7 +71,9 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
 //   mode 3: h = rmsnorm(x; nw2, eps2) -> hout;  xn = rmsnorm(h + x2[row / x2_div]; nw, eps) -> xout
 // (the same arithmetic as the ring GEMV's X_RMSNORM / X_NORM_ADD_NORM prologues).
 __global__ void __launch_bounds__(256) norm_rows_kernel(const NormRowsArgs a) {
+    if (threadIdx.x == 0) stamp_min(a.ts);
     pdl_wait();
+    if (threadIdx.x == 0) stamp_wait(a.ts);
     pdl_trigger();
     __shared__ float red[8];
     constexpr int PT = 12;  // D / 256
@@ -118,6 +120,10 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(const NormRowsArgs a) {
             a.xn[(size_t)r * a.D + i] = o;
             if (a.xout) a.xout[(size_t)r * a.D + i] = o;
         }
+    }
+    if (a.ts) {
+        __syncthreads();
+        if (tid == 0) stamp_max(a.ts + 3);
     }
 }
 

@@ -23,6 +23,7 @@ struct NormRowsArgs {
     float* xout;  // optional copy of xn
     float* hout;  // optional inner norm (mode 3)
     int D, mode;  // mode 1 rmsnorm, 3 norm-add-norm
+    unsigned long long* ts;  // optional debug timeline (kernel stamps [0..3])
 };
 int norm_rows(const NormRowsArgs& a, int rows, cudaStream_t s, bool pdl);
 cudaError_t advance_launch(int* cnt, int n, cudaStream_t s, bool pdl);

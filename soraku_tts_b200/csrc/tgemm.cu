@@ -520,6 +520,27 @@ bool tg_map(CUtensorMap* m, const float* p, int inner, int rows, int ld, int box
 }
 }  // namespace
 
+template <typename Kern>
+int tg_clusters(Kern* kern, size_t smem, int c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, c);
+    cfg.blockDim = dim3(TG_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = c;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    return n;
+}
+
 cudaError_t tgemm_prepare() {
     static bool done = false;
     if (done) return cudaSuccess;
@@ -537,23 +558,7 @@ cudaError_t tgemm_prepare() {
     cudaDeviceGetAttribute(&tg_n_sm, cudaDevAttrMultiProcessorCount, dev);
     tg_max_clusters[1] = tg_n_sm;
     for (int c = 2; c <= TG_MAX_SPLITS; ++c) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(1, 1, c);
-        cfg.blockDim = dim3(TG_THREADS);
-        cfg.dynamicSmemBytes = TG_SMEM;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = 1;
-        at[0].val.clusterDim.y = 1;
-        at[0].val.clusterDim.z = c;
-        cfg.attrs = at;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, tgemm_kernel, &cfg) != cudaSuccess) {
-            cudaGetLastError();
-            n = 0;
-        }
-        tg_max_clusters[c] = n;
+        tg_max_clusters[c] = tg_clusters(tgemm_kernel, TG_SMEM, c);
     }
     done = true;
     return cudaSuccess;
@@ -563,19 +568,21 @@ cudaError_t tgemm_prepare() {
 // else the most splits (<= 8, >= 4 stages each) for which one cluster per
 // tile is resident at once.
 int tgemm_splits(const GemmArgs& a) {
+    const int* mc = tg_max_clusters;
     const int tiles = ((a.N + TG_BN - 1) / TG_BN) * ((a.T + TG_BM - 1) / TG_BM);
     const int nst = a.K / TG_BK;
+    const int min_stages = 4;
     int ks;
     if (a.splits > 0) {
         ks = a.splits < TG_MAX_SPLITS ? a.splits : TG_MAX_SPLITS;
         if (ks > nst) ks = nst;
-        while (ks > 1 && tg_max_clusters[ks] < 1) --ks;
+        while (ks > 1 && mc[ks] < 1) --ks;
         return ks < 1 ? 1 : ks;
     }
     ks = tg_n_sm / tiles;
-    if (ks > nst / 4) ks = nst / 4;
+    if (ks > nst / min_stages) ks = nst / min_stages;
     if (ks > TG_MAX_SPLITS) ks = TG_MAX_SPLITS;
-    while (ks > 1 && tg_max_clusters[ks] < tiles) --ks;
+    while (ks > 1 && mc[ks] < tiles) --ks;
     return ks < 1 ? 1 : ks;
 }
 
@@ -586,6 +593,8 @@ cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl) {
     const cudaError_t pe = tgemm_prepare();
     if (pe != cudaSuccess) return pe;
     if (a.K % TG_BK != 0 || a.K <= 0 || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
+    // the FFMA kernel up to 16 rows (measured: at 32 rows the tcgen05 tile wins)
+    if (a.variant == 2 || (a.variant == 0 && a.T <= 16 && fgemm_supported(a))) return fgemm_launch(a, s, pdl);
     TgMaps tm;
     memset(&tm, 0, sizeof tm);
     bool ok = tg_map(&tm.a, a.A, a.K, a.T, a.lda, TG_BM);

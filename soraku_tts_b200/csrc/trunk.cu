@@ -479,6 +479,10 @@ extern "C" int skb_test_gemm(const float* x, const float* w, float* out, int M, 
     a.out = out;
     a.ldo = N;
     a.splits = splits;
+    if (tensor_cores < 0 || tensor_cores > 3) return fail(SKB_ERR_ARG, "test_gemm: tensor_cores %d", tensor_cores);
+    if (tensor_cores == 3 && (M > 32 || K % 256 != 0))
+        return fail(SKB_ERR_ARG, "test_gemm: the FFMA kernel takes at most 32 rows and K % 256 == 0");
+    a.variant = tensor_cores >= 2 ? tensor_cores - 1 : 0;
     const cudaError_t e = tensor_cores ? tgemm_launch(a, stream, false) : sgemm_launch(a, stream, false);
     return e == cudaSuccess ? SKB_OK : fail(SKB_ERR_CUDA, "test_gemm: %s", cudaGetErrorString(e));
 }

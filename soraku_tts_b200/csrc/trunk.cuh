@@ -75,10 +75,16 @@ struct GemmArgs {
     int mode;  // 0 store, 1 resid, 2 bias, 3 swiglu
     int* err;  // optional: set when a wait timed out (tensor-core GEMM)
     int splits;  // tensor-core GEMM: K splits per output tile (0 = chosen by occupancy)
-    // tensor-core GEMM debug timeline (null: off): [0..3] as for every
-    // kernel, [4] latest / [8] earliest first stage at the MMA, [5] latest
+    // kernel: 0 chooses by rows (the FFMA kernel for T <= 16 when it takes
+    // the shape, else the tensor-core GEMM), 1 the tensor-core GEMM, 2 the
+    // FFMA kernel (T <= 32)
+    int variant;
+    // debug timeline (null: off): [0..3] as for every kernel; tensor-core
+    // GEMM: [4] latest / [8] earliest first stage at the MMA, [5] latest
     // all-MMAs-done, [6] latest result staged (after the cluster barrier),
-    // [7] latest output stores issued
+    // [7] latest output stores issued; FFMA kernel: [4] latest first chunk
+    // landed, [5] all chunks consumed, [6] partials reduced, [8 + c] / [12 +
+    // c] chunk c (< 4) landed / consumed
     unsigned long long* ts;
 };
 

@@ -19,8 +19,12 @@ cudaError_t prefill_embed_launch(const PrefillTok* toks, int T, const float* emb
 cudaError_t speaker_launch(const float* v, int SD, const float* W, int D, const float* slot,
                            float* out, cudaStream_t s);
 cudaError_t sgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl = false);
-// 3xTF32 tcgen05 GEMM (tgemm.cu); K a multiple of 32.
+// The batched / prefill GEMM (GemmArgs::variant picks the kernel; 0 =
+// by rows): the FP32 FFMA kernel of fgemm.cu for T <= 16, else the 3xTF32
+// tcgen05 GEMM of tgemm.cu; K a multiple of 32 (256 for the FFMA kernel).
 cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl = false);
+bool fgemm_supported(const GemmArgs& a);
+cudaError_t fgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl = false);
 cudaError_t prefill_qk_launch(const float* qkv, int ld, const PrefillTok* toks, int T,
                               const float* qn, const float* kn, float eps, const float* rc,
                               const float* rs, int H, const KVLayout& kv, int layer, float* Qo,
