@@ -34,7 +34,7 @@ namespace skb {
 constexpr int RG_CWARPS = 8;                      // consumer warps
 constexpr int RG_THREADS = 32 * (RG_CWARPS + 1);  // + the producer warp
 constexpr int RG_SLOT = 24 * 1024;                // ring slot bytes
-constexpr int RG_MAX_SLOTS = 4;
+constexpr int RG_MAX_SLOTS = 5;
 constexpr int RG_HEAD = 256;                      // mbarriers + flags
 // Dynamic shared memory per CTA: at most this much, so that two CTAs (of this
 // kernel and its neighbour in the frame) fit in one SM's 228 KB.  Inner size
@@ -43,7 +43,12 @@ constexpr int RG_HEAD = 256;                      // mbarriers + flags
 // neighbours (gate/up, QKV: 104 KB each) still fit beside it.
 constexpr size_t RG_SMEM_BUDGET = 112 * 1024;
 constexpr size_t RG_SMEM_BUDGET_K3072 = 121 * 1024;
-constexpr size_t RG_SMEM_MAX = RG_SMEM_BUDGET_K3072;
+// SwiGLU at inner size 1024 (the trunk gate/up, 170 KB of weights per CTA at
+// batch 1) gets a fifth slot: its neighbours -- the O projection (3 slots: a
+// ring is never deeper than a CTA's chunk count) and the down projection
+// (96 KB) -- still fit beside it in one SM.
+constexpr size_t RG_SMEM_BUDGET_SWIGLU = 129 * 1024;
+constexpr size_t RG_SMEM_MAX = RG_SMEM_BUDGET_SWIGLU;
 constexpr int RG_EPI_MAX = 256;  // staged residual / bias values per CTA
 
 struct RgHead {
@@ -474,11 +479,17 @@ inline RgPlan rgemv_plan(int N, int K, int M, int EM, int want) {
     const int G0 = want < NU0 ? (want < 1 ? 1 : want) : NU0;
     p.ks = p.kq > 8 && EM != E_SWIGLU && (NU0 + G0 - 1) / G0 <= RG_KS_UNITS && M * RG_KS_UNITS <= 32;
     const size_t xbytes = p.ks ? 0 : (size_t)M * p.kq * 128 * 4;
-    const size_t budget = p.kq == 24 ? RG_SMEM_BUDGET_K3072 : RG_SMEM_BUDGET;
+    const size_t budget = p.kq == 24 ? RG_SMEM_BUDGET_K3072
+                                     : (EM == E_SWIGLU && p.kq == 8 ? RG_SMEM_BUDGET_SWIGLU : RG_SMEM_BUDGET);
     const size_t avail = budget > RG_HEAD + xbytes + 2 * RG_SLOT ? budget - RG_HEAD - xbytes : 2 * RG_SLOT;
     p.slots = (int)(avail / RG_SLOT);
     if (p.slots > RG_MAX_SLOTS) p.slots = RG_MAX_SLOTS;
     if (p.slots < 2) p.slots = 2;
+    // no deeper than the chunks of the largest CTA slice: unused slots would
+    // only keep a neighbouring kernel's CTA off the SM
+    const int units = (NU0 + G0 - 1) / G0, upc = RG_SLOT / unit_bytes;
+    const int nch = (units + upc - 1) / upc;
+    if (p.slots > nch) p.slots = nch < 1 ? 1 : nch;
     p.smem = RG_HEAD + xbytes + (size_t)p.slots * RG_SLOT;
     const int NU = (EM == E_SWIGLU) ? N / 2 : N;
     p.grid = want < NU ? want : NU;
