@@ -359,7 +359,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     // 32*(w%4).. (tile rows) and result columns 64*(w/4).. as D[c] + D[128+c]
     const int rq = warp & 3, hf = warp >> 2;
     float* acc_s = reinterpret_cast<float*>(base);  // the ring is idle now
-    {
+    // rows of X this tile holds (a batch of 32 or 64 rows fills part of the
+    // 128-row tile): staging and the split-K reduction skip the rest
+    const int rows_here = a.T - m0 < TG_BM ? a.T - m0 : TG_BM;
+    if (32 * rq < rows_here) {
         const uint32_t lrow = tmem + ((uint32_t)(32 * rq) << 16);
         float* row = acc_s + (32 * rq + lane) * TG_OUT_LD;
 #pragma unroll 1
@@ -395,7 +398,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     // split tile owns groups [z*G/ks, (z+1)*G/ks)
     const bool glu = a.mode == 3;
     const int per_row = glu ? TG_BN / 8 : TG_BN / 4;
-    const int G = TG_BM * per_row;
+    const int G = rows_here * per_row;
     const int g_lo = split ? (int)((long long)z * G / ks) : 0;
     const int g_hi = split ? (int)((long long)(z + 1) * G / ks) : G;
     const bool vec_out = ((a.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0);
