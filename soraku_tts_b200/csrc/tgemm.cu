@@ -318,10 +318,18 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     } else {  // X rows -> TMEM (warp w owns TMEM lanes 32*(w%4)..)
         const int r = 32 * (warp & 3) + lane;
         const uint32_t lane_addr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        // a warp whose 32 rows all lie past the batch moves nothing (those
+        // TMEM lanes only feed result rows that are never stored) but still
+        // paces its arrivals by the stages
+        const bool moves = 32 * (warp & 3) < a.T - m0;
         for (int i = 0; i < nloc; ++i) {
             const int s = i % TG_STAGES;
             if (lane == 0 && !mbar_wait(&full[s], (uint32_t)(i / TG_STAGES) & 1u, a.err)) err = 1;
             __syncwarp();
+            if (!moves) {
+                if (lane == 0) tg_arrive(&ready[s]);
+                continue;
+            }
             // The stage's TMEM buffer is free: its previous MMAs completed
             // before the producer refilled this slot.
             const unsigned char* raw = base + s * TG_STAGE;
