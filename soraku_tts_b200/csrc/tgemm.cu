@@ -181,6 +181,11 @@ __device__ __forceinline__ float4 tg_ld_peer4(uint32_t local, uint32_t rank) {
     return v;
 }
 
+// PART: a batch of fewer than 128 rows (one row tile, partly filled): the
+// X movers, the result staging and the split-K reduction skip the rows past
+// it.  Full tiles run without those tests (they cost the full-tile K loop
+// several per cent in measurement).
+template <bool PART>
 __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, const __grid_constant__ TgMaps tm) {
     extern __shared__ unsigned char tg_raw[];
     // 1024-byte aligned stage buffers (the swizzle pattern repeats every 1024 B)
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
         // a warp whose 32 rows all lie past the batch moves nothing (those
         // TMEM lanes only feed result rows that are never stored) but still
         // paces its arrivals by the stages
-        const bool moves = 32 * (warp & 3) < a.T - m0;
+        const bool moves = !PART || 32 * (warp & 3) < a.T - m0;
         for (int i = 0; i < nloc; ++i) {
             const int s = i % TG_STAGES;
             if (lane == 0 && !mbar_wait(&full[s], (uint32_t)(i / TG_STAGES) & 1u, a.err)) err = 1;
@@ -369,8 +374,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemm_kernel(const GemmArgs a, 
     float* acc_s = reinterpret_cast<float*>(base);  // the ring is idle now
     // rows of X this tile holds (a batch of 32 or 64 rows fills part of the
     // 128-row tile): staging and the split-K reduction skip the rest
-    const int rows_here = a.T - m0 < TG_BM ? a.T - m0 : TG_BM;
-    if (32 * rq < rows_here) {
+    const int rows_here = PART ? (a.T - m0 < TG_BM ? a.T - m0 : TG_BM) : TG_BM;
+    if (!PART || 32 * rq < rows_here) {
         const uint32_t lrow = tmem + ((uint32_t)(32 * rq) << 16);
         float* row = acc_s + (32 * rq + lane) * TG_OUT_LD;
 #pragma unroll 1
@@ -555,7 +560,8 @@ int tg_clusters(Kern* kern, size_t smem, int c) {
 cudaError_t tgemm_prepare() {
     static bool done = false;
     if (done) return cudaSuccess;
-    cudaError_t e = set_smem_attrs(tgemm_kernel, TG_SMEM);
+    cudaError_t e = set_smem_attrs(tgemm_kernel<false>, TG_SMEM);
+    if (e == cudaSuccess) e = set_smem_attrs(tgemm_kernel<true>, TG_SMEM);
     if (e != cudaSuccess) return e;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
     e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&tg_encode), cudaEnableDefault,
@@ -569,7 +575,7 @@ cudaError_t tgemm_prepare() {
     cudaDeviceGetAttribute(&tg_n_sm, cudaDevAttrMultiProcessorCount, dev);
     tg_max_clusters[1] = tg_n_sm;
     for (int c = 2; c <= TG_MAX_SPLITS; ++c) {
-        tg_max_clusters[c] = tg_clusters(tgemm_kernel, TG_SMEM, c);
+        tg_max_clusters[c] = tg_clusters(tgemm_kernel<false>, TG_SMEM, c);
     }
     done = true;
     return cudaSuccess;
@@ -642,7 +648,7 @@ cudaError_t tgemm_launch(const GemmArgs& a, cudaStream_t s, bool pdl) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, tgemm_kernel, a, tm);
+    return a.T < TG_BM ? cudaLaunchKernelEx(&cfg, tgemm_kernel<true>, a, tm) : cudaLaunchKernelEx(&cfg, tgemm_kernel<false>, a, tm);
 }
 
 }  // namespace skb
