@@ -129,6 +129,7 @@ enum : int { PH_GEMV = 0, PH_ATTN = 1 };
 struct Phase {
     int kind;
     int xm, em;
+    int pre_normed;  // batched rows: the previous sampler wrote this phase's normed rows
     int sample;
     int n_req;
     GemvArgs g;
@@ -252,6 +253,7 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
             a.out = e->act;
             a.ldo = e->I;
             phases.push_back(gemv_phase(a, X_NORM_ADD_NORM, E_SWIGLU));
+            phases.back().pre_normed = (R >= e->gemm_min_rows && q > 0 && D <= 1024) ? 1 : 0;
         }
         {  // D_down
             GemvArgs a = gemv_args_plain(e->act, e->I, D, e->I);
@@ -292,6 +294,17 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
             a.bos = e->m.bos_id;
             a.pad = e->m.pad_id;
             a.eos = e->m.eos_id;
+            // batched rows: the sampler also forms the next step's depth
+            // input rows (replacing that step's row-norm launch)
+            if (R >= e->gemm_min_rows && q < e->Q - 1 && D <= 1024) {
+                a.fn_w = e->m.final_norm;
+                a.fn_eps = e->m.rms_eps;
+                a.ni_w = e->m.depth_norm_in;
+                a.ni_eps = e->m.depth_eps;
+                a.xn = e->xn;
+                a.xout = e->abuf;
+                a.hout = e->hidden;
+            }
             Phase& cls = phases.back();
             cls.sample = 1;
             cls.n_req = n_active;
@@ -382,7 +395,7 @@ std::vector<Phase> build_phases(skb_engine* e, int n_active) {
 // rows, then the position advance of the frame's last GEMV.
 void gemm_rows_nodes(skb_engine* e, const Phase& ph, int R, std::vector<Node>& nodes) {
     const GemvArgs& g = ph.g;
-    if (ph.xm != X_PLAIN) {
+    if (ph.xm != X_PLAIN && !ph.pre_normed) {
         NormRowsArgs na = {};
         na.x = g.x;
         na.ldx = g.ldx;

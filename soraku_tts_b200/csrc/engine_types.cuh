@@ -28,6 +28,15 @@ struct DepthSampleArgs {
     int64_t* hist;       // [n_req][max_frames][Q]
     int max_frames;
     int bos, pad, eos;
+    // Optional (batched rows, codebooks before the last): the next depth
+    // step's input rows, a = norm_in(final_norm(x) + prefix) with the updated
+    // prefix, written here instead of by a row-norm launch: xn and xout get a,
+    // hout the final-normed x (null: not done)
+    const float* fn_w;  // final norm weight [D]
+    float fn_eps;
+    const float* ni_w;  // depth norm_in weight [D]
+    float ni_eps;
+    float *xn, *xout, *hout;  // [R][D]
     PrefetchList pf;
     unsigned long long* ts;  // optional debug timeline [4]
 };
@@ -58,6 +67,61 @@ __device__ __forceinline__ SampleJob depth_sample_job(const DepthSampleArgs& a, 
     return J;
 }
 
+// Block sum of one float per thread (256 threads); red: 8 floats of shared memory.
+template <class Sync>
+__device__ __forceinline__ float depth_block_sum(float v, float* red) {
+    v = warp_sum(v);
+    Sync::sync();  // red is free (its last readers are done)
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    Sync::sync();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w];
+    return t;
+}
+
+// The next depth step's input rows of request r (its rows_per_req rows):
+// h = fn_w * (x * inv_rms(x)), v = h + prefix, a = ni_w * (v * inv_rms(v)),
+// the operations and order of the row-norm kernel they replace.  pv: this
+// thread's prefix values (columns tid + 256 j).
+template <class Sync>
+__device__ void depth_next_rows(const DepthSampleArgs& a, int r, const float (&pv)[4], float* red) {
+    const int tid = threadIdx.x;
+    for (int rr = 0; rr < a.rows_per_req; ++rr) {
+        const size_t row = (size_t)r * a.rows_per_req + rr;
+        float v[4];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + SAMPLER_THREADS * j;
+            v[j] = i < a.D ? __ldcg(a.x + row * a.D + i) : 0.f;
+            ss += v[j] * v[j];
+        }
+        const float inv1 = rsqrtf(depth_block_sum<Sync>(ss, red) / (float)a.D + a.fn_eps);
+        ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + SAMPLER_THREADS * j;
+            if (i < a.D) {
+                const float h = a.fn_w[i] * (v[j] * inv1);
+                if (a.hout) a.hout[row * a.D + i] = h;
+                v[j] = h + pv[j];
+            }
+            ss += v[j] * v[j];
+        }
+        const float inv2 = rsqrtf(depth_block_sum<Sync>(ss, red) / (float)a.D + a.ni_eps);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = tid + SAMPLER_THREADS * j;
+            if (i < a.D) {
+                const float o = a.ni_w[i] * (v[j] * inv2);
+                a.xn[row * a.D + i] = o;
+                if (a.xout) a.xout[row * a.D + i] = o;
+            }
+        }
+    }
+}
+
 // One request's sampling step for codebook a.q (job J from depth_sample_job)
 // and its epilogue: the code goes to the current-frame and history buffers,
 // the prefix grows by table[q][code] * scale, and after the last codebook the
@@ -81,7 +145,23 @@ __device__ void depth_sample_body(const DepthSampleArgs& a, int r, const SampleJ
     float* pr = a.prefix + (size_t)r * a.D;
     if (a.q < a.Q - 1) {
         const float* trow = a.table + ((size_t)a.q * a.V + code) * a.D;
-        for (int i = tid; i < a.D; i += SAMPLER_THREADS) pr[i] = __ldcg(pr + i) + trow[i] * a.scale;
+        if (a.xn == nullptr) {
+            for (int i = tid; i < a.D; i += SAMPLER_THREADS) pr[i] = __ldcg(pr + i) + trow[i] * a.scale;
+        } else {
+            // the updated prefix stays in registers for the next step's rows
+            constexpr int PT = 4;  // D / 256 (D <= 1024)
+            float pv[PT];
+#pragma unroll
+            for (int j = 0; j < PT; ++j) {
+                const int i = tid + SAMPLER_THREADS * j;
+                pv[j] = 0.f;
+                if (i < a.D) {
+                    pv[j] = __ldcg(pr + i) + trow[i] * a.scale;
+                    pr[i] = pv[j];
+                }
+            }
+            depth_next_rows<Sync>(a, r, pv, reinterpret_cast<float*>(smem));
+        }
     } else {
         if (tid < a.Q) codes_s[tid] = (tid == a.q) ? code : (int)__ldcg(a.cur_codes + (size_t)r * a.Q + tid);
         Sync::sync();
