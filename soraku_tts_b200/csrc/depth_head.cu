@@ -210,7 +210,12 @@ __device__ void dh_producer(const DepthArgs& A, DhHead& hd, float* ring, float* 
         if (k < DH_SLOTS) return true;
         return dh_mbar_wait(&hd.empty[k % DH_SLOTS], ((k / DH_SLOTS) - 1u) & 1u, A);
     };
+    // table[0]'s slice into L2 now, table[q+1]'s at the start of step q: the
+    // classifier phase then streams its rows from L2 rather than HBM
+    if (c1 > c0) bulk_prefetch_l2(A.table + (size_t)c0 * DH_D, (unsigned)(c1 - c0) * DH_D * 4u);
     for (int q = 0; q < A.Q; ++q) {
+        if (q + 1 < A.Q && c1 > c0)
+            bulk_prefetch_l2(A.table + ((size_t)(q + 1) * A.V + c0) * DH_D, (unsigned)(c1 - c0) * DH_D * 4u);
         for (int r = d0; r < d1; r += DH_DN_UPC) {
             if (!slot_free(g)) goto done;
             const int n = min(DH_DN_UPC, d1 - r);
