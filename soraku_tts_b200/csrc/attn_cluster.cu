@@ -49,6 +49,7 @@ struct AtcSmem {
     float vn[128];
     float p[2][PMAX + 4];  // scores, then probabilities (+ the new position)
     float mr[2], lr[2];    // per-round block max / sum
+    float wmx[8][2], wsm[8][2];  // double-buffered variant: per-round, per-warp score max / probability sum
     uint64_t bar[NBUF];
     uint64_t merge_bar;  // rank 0: every CTA's partial has arrived
     int err;
@@ -234,6 +235,7 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             ++n_waited[b];
         }
         if (rd == 0) tl[1] = a.ts ? globaltimer_ns() : 0;
+        float wm0 = -INFINITY, wm1 = -INFINITY;  // this warp's score max per head (double-buffered variant)
         for (int i0 = warp * 4; i0 < ns; i0 += 32) {
             const int i = i0 + sg;
             const float4* kr = reinterpret_cast<const float4*>(i < nc ? sm.k[b][i < nc ? i : 0] : sm.kn);
@@ -261,11 +263,54 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
                 sm.p[0][i] = s0;
                 if (n_rep > 1) sm.p[1][i] = s1;
             }
+            if (NBUF > 1 && i < ns) {
+                wm0 = fmaxf(wm0, s0);
+                wm1 = fmaxf(wm1, s1);
+            }
+        }
+        if constexpr (NBUF > 1) {
+            wm0 = warp_max(wm0);
+            wm1 = warp_max(wm1);
+            if (lane == 0) {
+                sm.wmx[warp][0] = wm0;
+                sm.wmx[warp][1] = wm1;
+            }
         }
         __syncthreads();
         if (rd == 0) tl[2] = a.ts ? globaltimer_ns() : 0;
-        // per-head max (warp h), then probabilities and their sum (warp h)
-        if (warp < n_rep) {
+        if constexpr (NBUF > 1) {
+            // the round's max per head (warps in order); every warp turns its
+            // own slots into probabilities: lane l takes head l / 16 and the
+            // warp's slot number l % 16 (slots warp*4 + 32k + j, k, j < 4)
+            static_assert(PMAX + 1 <= 128, "16 lanes per head cover a warp's slots only below 128");
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                mx0 = fmaxf(mx0, sm.wmx[w][0]);
+                mx1 = fmaxf(mx1, sm.wmx[w][1]);
+            }
+            const float mn0 = fmaxf(m_run[0], mx0), mn1 = n_rep > 1 ? fmaxf(m_run[1], mx1) : -INFINITY;
+            const int h = lane >> 4, t = lane & 15;
+            const int i = warp * 4 + 32 * (t >> 2) + (t & 3);
+            const float mh = h == 0 ? mn0 : mn1;
+            float e = 0.f;
+            if (h < n_rep && i < ns) {
+                e = (mh == -INFINITY) ? 0.f : expf(sm.p[h][i] - mh);
+                sm.p[h][i] = e;
+            }
+#pragma unroll
+            for (int o = 8; o >= 1; o >>= 1) e += __shfl_xor_sync(FULL, e, o);  // within each half-warp
+            if (t == 0) sm.wsm[warp][h] = e;
+            __syncthreads();
+            if (tid < 2) {  // the round's (max, sum) per head, sums in warp order
+                float sum = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) sum += sm.wsm[w][tid];
+                sm.mr[tid] = tid == 0 ? mn0 : mn1;
+                sm.lr[tid] = sum;
+            }
+        } else if (warp < n_rep) {
+            // per-head max (warp h), then probabilities and their sum (warp h)
             float mx = -INFINITY;
             for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, sm.p[warp][i]);
             mx = warp_max(mx);
