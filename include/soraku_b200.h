@@ -126,7 +126,8 @@ int skb_cfg_sample(const float *logits, int rows_per_req, int n_req, int V,
  *   part       scratch [rows * n_kv_heads * splits * (n_heads/n_kv_heads) * (head_dim + 2)]
  *   tickets    scratch int32 [rows * n_kv_heads], zero before the call (left zero)
  *   out        device [rows, n_heads * head_dim]
- * head_dim must be 128 and n_heads / n_kv_heads 1 or 2. */
+ * head_dim must be 128 and n_heads / n_kv_heads 1 or 2; qkv, the norm weights,
+ * the RoPE tables and kv_pool 16-byte aligned. */
 int skb_decode_attention(const float *qkv, int rows, int n_heads, int n_kv_heads, int head_dim,
                          const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
                          const float *rope_sin, int max_len, const int32_t *pos, float *kv_pool,

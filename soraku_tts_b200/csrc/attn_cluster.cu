@@ -157,8 +157,12 @@ __global__ void __launch_bounds__(ATC_THREADS) decode_attn_cluster_kernel(const 
             const int p0 = pb + b * PMAX;
             if (atc_stage(a, r, g, p0, min(cend, p0 + PMAX), sm, b) > 0) ++n_issued[b];
         }
-        // later rounds (long contexts): into L2 now, into shared memory later
-        for (int p = pb + NBUF * PMAX; p < cend;) {
+        // later rounds (long contexts) of the single-buffered variant: into
+        // L2 now, into shared memory later.  The double-buffered variant
+        // streams without it: its second buffer already keeps copies in
+        // flight, and L2 prefetches running ahead of bulk copies slowed that
+        // stream (92.4 against 97.9 us for 256 rows x 8 kv heads, measured)
+        for (int p = pb + NBUF * PMAX; NBUF == 1 && p < cend;) {
             const int end = min(cend, ((p >> a.kv.page_log2) + 1) << a.kv.page_log2);
             const float* kb = a.kv.at(a.layer, r, p, 0, g);
             const float* vb = a.kv.at(a.layer, r, p, 1, g);

@@ -412,6 +412,9 @@ int decode_attention_check(const float* qkv, int rows, int H, int KVH, int hd, c
         return fail(SKB_ERR_ARG, "decode_attention: bad sizes");
     if (page_size < 1 || (page_size & (page_size - 1)) != 0 || (long long)max_pages * page_size < max_len)
         return fail(SKB_ERR_ARG, "decode_attention: page_size must be a power of two covering max_len");
+    // the kernels read these with 16-byte loads and bulk copies
+    if (((uintptr_t)qkv | (uintptr_t)rc | (uintptr_t)rs | (uintptr_t)kv_pool | (uintptr_t)qn | (uintptr_t)kn) & 15u)
+        return fail(SKB_ERR_ARG, "decode_attention: qkv, norm weights, RoPE tables and kv_pool must be 16-byte aligned");
     return SKB_OK;
 }
 
